@@ -1,0 +1,519 @@
+"""Paged decode benchmark: KV append + paged GQA decode over every layer of one
+decode step, on 1..N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 70b|7b]
+                    [--impl ours|reference] [--no-e2e] [--no-cpu-baseline]
+
+Workloads (synthetic, seeded; fp16 K/V/Q drawn from N(0, 0.5^2)):
+  70b  Llama-2-70B-shaped GQA decode: 64 query heads, 8 KV heads, head dim 128,
+       80 layers, batch 64, context lengths lognormal (median 2048, sigma 0.6)
+       clipped to [256, 8192], 16-token pages in a random block table.  At N
+       GPUs each rank holds 8/N KV heads (and their 64/N query heads) of every
+       sequence; the per-layer outputs are all-gathered with NCCL on a
+       communication stream that overlaps the next layer.
+  7b   Llama-2-7B decode: 32/32 heads, head dim 128, 32 layers, batch 32,
+       contexts uniform in [128, 4096], pool 1.2x the tokens; sequences are
+       sharded across ranks (no collective).
+
+One step = for every layer: append one token per sequence (K1), then decode
+attention over the whole context (K2: split-K decode + merge).  Timed with CUDA
+events between barriers, max over ranks.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged decode-attn tokens/s & HBM GB/s (% of B200 peak) at 1/2/4/8 B200"
+PAGE = 16
+
+
+# ----------------------------------------------------------------------------- workload
+
+def workload(name: str):
+    if name == "70b":
+        rng = np.random.Generator(np.random.PCG64(2048))
+        B, sigma = 64, 0.6
+        ctx = np.clip(np.round(np.exp(rng.normal(math.log(2048), sigma, B))), 256, 8192).astype(np.int64)
+        return dict(name="llama2-70b-gqa-decode", B=B, Hq=64, Hkv=8, D=128, L=80, ctx=ctx, shard="head",
+                    desc="Llama-2-70B GQA decode: B=64, Hq=64, Hkv=8, D=128, L=80, 16-token pages, "
+                         "ctx lognormal(median 2048, sigma 0.6) clipped [256, 8192], random block table",
+                    sigma=sigma, seed=2048)
+    if name == "7b":
+        rng = np.random.Generator(np.random.PCG64(4096))
+        B = 32
+        ctx = rng.integers(128, 4097, B).astype(np.int64)
+        return dict(name="llama2-7b-decode", B=B, Hq=32, Hkv=32, D=128, L=32, ctx=ctx, shard="seq",
+                    desc="Llama-2-7B decode: B=32, Hq=Hkv=32, D=128, L=32, 16-token pages, "
+                         "ctx uniform [128, 4096], pool 1.2x tokens, random block table",
+                    seed=4096)
+    raise SystemExit("unknown config " + name)
+
+
+def layout(ctx, seed, slack=1.2):
+    """Random physical pages for contexts ctx (+1 appended token each)."""
+    rng = np.random.Generator(np.random.PCG64(seed + 1))
+    lens = ctx + 1
+    need = (lens + PAGE - 1) // PAGE
+    num_pages = int(math.ceil(slack * need.sum()))
+    perm = rng.permutation(num_pages).astype(np.int32)
+    width = int(need.max())
+    bt = np.full((len(ctx), width), -1, np.int32)
+    off = 0
+    for b, k in enumerate(need):
+        bt[b, :k] = perm[off:off + k]
+        off += k
+    return bt, num_pages
+
+
+def algorithmic_bytes(ctx, Hq, Hkv, D):
+    """Bytes one layer of one step must move (counted once): K/V read, new K/V
+    read+write, Q read + O write, block-table reads."""
+    lens = ctx + 1
+    kv = int((2 * lens * Hkv * D * 2).sum())
+    new = len(ctx) * 2 * Hkv * D * 2 * 2
+    qo = len(ctx) * 2 * Hq * D * 2
+    table = int((4 * ((lens + PAGE - 1) // PAGE)).sum())
+    return dict(decode=kv + qo + table, append=new, total=kv + new + qo + table)
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            self.path = "/tmp/vk_clocks_%d_%d.csv" % (os.getpid(), self.device)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- cpu baseline
+
+def cpu_decode_sample(wl, bt, ctx, Hkv, Hq, seqs, nthreads, host_pages=None):
+    """Times the oracle port of the reference's golden attention (decode row,
+    block-table gather) on one layer of the given sequences.  Returns seconds."""
+    import oracle
+    D = wl["D"]
+    lens = (ctx + 1).astype(np.int32)
+    sub_bt = bt[seqs]
+    need = (lens[seqs] + PAGE - 1) // PAGE
+    # compact host pool holding only the sampled sequences' pages of one layer
+    n_pages = int(need.sum())
+    g = oracle.Geom(1, Hkv, D, PAGE, n_pages)
+    rng = np.random.Generator(np.random.PCG64(99))
+    if host_pages is None:
+        pool = (rng.standard_normal(g.pool_shape(), dtype=np.float32) * 0.5).astype(np.float16)
+    else:
+        pool = host_pages
+    cbt = np.full((len(seqs), sub_bt.shape[1]), -1, np.int32)
+    off = 0
+    for i, k in enumerate(need):
+        cbt[i, :k] = np.arange(off, off + k, dtype=np.int32)
+        off += k
+    q = (rng.standard_normal((len(seqs), Hq, D), dtype=np.float32) * 0.5).astype(np.float16)
+    t0 = time.perf_counter()
+    oracle.decode_paged(pool.view(np.uint16), g, 0, q.view(np.uint16), cbt, lens[seqs], nthreads=nthreads)
+    return time.perf_counter() - t0
+
+
+def run_reference_arm(args, wl):
+    """The reference's CPU implementation of the path (oracle port of its golden
+    cpu_attention, decode row over the paged gather) on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ctx = wl["ctx"]
+    bt, _ = layout(ctx, wl["seed"])
+    threads = os.cpu_count() or 1
+    # bounded sample per step: one layer of a quarter of the sequences (all heads)
+    rng = np.random.Generator(np.random.PCG64(7))
+    seqs = np.sort(rng.choice(wl["B"], max(1, wl["B"] // 4), replace=False))
+    frac = float((ctx[seqs] + 1).sum()) / float((ctx + 1).sum())
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = cpu_decode_sample(wl, bt, ctx, wl["Hkv"], wl["Hq"], seqs, threads)
+        if i >= args.warmup:
+            times.append(t)
+    per_layer = statistics.median(times) / frac
+    step_s = per_layer * wl["L"]
+    value = wl["B"] / step_s
+    sample = ("1 of %d layers, %d of %d sequences (all %d heads) per step; step time extrapolated "
+              "x%d layers / %.3f of the tokens" % (wl["L"], len(seqs), wl["B"], wl["Hq"], wl["L"], frac))
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": wl["desc"], "shard": wl["shard"]},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="70b", choices=["70b", "7b"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pps", type=int, default=0, help="override decode pages per split (0 = auto)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    wl = workload(args.config)
+    if args.impl == "reference":
+        return run_reference_arm(args, wl)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit("WORLD_SIZE %d != --gpus %d" % (world, args.gpus))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    import vulcan_b200 as vk
+
+    B, Hq, Hkv, D, L = wl["B"], wl["Hq"], wl["Hkv"], wl["D"], wl["L"]
+    ctx_all = wl["ctx"]
+    bt_all, num_pages_all = layout(ctx_all, wl["seed"])
+    if wl["shard"] == "head":
+        if Hkv % world:
+            raise SystemExit("KV heads %d not divisible by %d GPUs" % (Hkv, world))
+        hkv_l, hq_l = Hkv // world, Hq // world
+        seqs = np.arange(B)
+        ctx, bt, num_pages = ctx_all, bt_all, num_pages_all
+    else:
+        # sequence sharding balanced by tokens: greedy longest-first onto the least-loaded rank
+        order = np.argsort(-ctx_all, kind="stable")
+        loads = [0] * world
+        owner = np.zeros(B, np.int64)
+        for i in order:
+            r = int(np.argmin(loads))
+            owner[i] = r
+            loads[r] += int(ctx_all[i] + 1)
+        seqs = np.nonzero(owner == rank)[0]
+        hkv_l, hq_l = Hkv, Hq
+        ctx = ctx_all[seqs]
+        bt, num_pages = layout(ctx, wl["seed"] + 17 * rank)
+    Bl = len(seqs)
+    lens = (ctx + 1).astype(np.int32)
+    max_len = int(lens.max())
+
+    # --- pool and inputs on the device
+    pool = vk.PagedKVPool(L, hkv_l, D, num_pages, own_memory=False, zero=False)
+    if args.pps:
+        pool.set_split(args.pps)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    flat = pool.storage.view(torch.float16)
+    chunk = 1 << 28
+    for s in range(0, flat.numel(), chunk):
+        part = flat[s:s + chunk]
+        part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    bt_d = torch.from_numpy(bt).to(dev)
+    pos_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    lens_d = torch.from_numpy(lens).to(dev)
+    q = (torch.randn(L, Bl, hq_l, D, device=dev, generator=gen) * 0.5).half()
+    kn = (torch.randn(L, Bl, 1, hkv_l, D, device=dev, generator=gen) * 0.5).half()
+    vn = (torch.randn(L, Bl, 1, hkv_l, D, device=dev, generator=gen) * 0.5).half()
+    out = torch.empty(L, Bl, hq_l, D, device=dev, dtype=torch.float16)
+    ws = pool.workspace(Bl, hq_l, max_len)
+    gathered = None
+    comm = None
+    if world > 1 and wl["shard"] == "head":
+        gathered = torch.empty(L, world, Bl, hq_l, D, device=dev, dtype=torch.float16)
+        comm = torch.cuda.Stream(device=dev)
+    compute = torch.cuda.current_stream(dev)
+    merge_launched = 1 if pool.workspace_size(Bl, hq_l, max_len) > 0 else 0
+    launches_per_step = L * (2 + merge_launched)
+
+    dec_events = []
+
+    def step(record=False):
+        evs = []
+        for l in range(L):
+            pool.append(l, kn[l], vn[l], bt_d, pos_d)
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(compute)
+            pool.decode(l, q[l], bt_d, lens_d, max_len, out=out[l], workspace=ws)
+            if record:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(compute)
+                evs.append((e0, e1))
+            if gathered is not None:
+                ev = torch.cuda.Event()
+                ev.record(compute)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(gathered[l].view(-1), out[l].view(-1))
+        if gathered is not None:
+            compute.wait_stream(comm)
+        if record:
+            dec_events.extend(evs)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    pool.check()  # no device errors during warm-up
+    barrier()
+
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t_start.record(compute)
+        for _ in range(args.steps):
+            step(record=True)
+        t_end.record(compute)
+        barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
+    dec_avg_ms = sum(dec_ms) / len(dec_ms)
+    clocks = clk.summary()
+
+    # --- algorithmic bytes (this rank's share) and roofline of the decode launch
+    ab_local = algorithmic_bytes(ctx, hq_l, hkv_l, D)
+    peak, peak_kind = measured_peaks()
+    achieved = ab_local["decode"] / (dec_avg_ms * 1e-3) / 1e9
+    ab_job = algorithmic_bytes(ctx_all, Hq, Hkv, D)
+    job_gbs = ab_job["total"] * L / (ms_step * 1e-3) / 1e9
+    tokens_s = B / (ms_step * 1e-3)
+
+    # --- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world,
+                      gathered, comm)
+        e2e["value"] = B / (e2e.pop("ms_step") * 1e-3)
+
+    # --- CPU baseline (rank 0 at N=1 only): oracle port, 1 thread, bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rng = np.random.Generator(np.random.PCG64(5))
+        sample = np.sort(rng.choice(Bl, max(1, Bl // 8), replace=False))
+        frac = float(lens[sample].sum()) / float(lens.sum())
+        t_cpu = cpu_decode_sample(wl, bt, ctx, hkv_l, hq_l, sample, 1)
+        step_cpu = t_cpu / frac * L
+        cpu = {"value": B / step_cpu, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": "oracle port of the reference's golden attention, 1 thread: 1 of %d layers, "
+                         "%d of %d sequences (all heads); extrapolated x%d layers / %.3f of the tokens "
+                         "(%.1f s measured)" % (L, len(sample), Bl, L, frac, t_cpu)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,0.5^2) fp16 K/V/Q, random block tables)",
+            "config": {"workload": wl["desc"], "shard": wl["shard"] if world > 1 else "none",
+                       "parallelism": ("kv-head shard x%d + NCCL allgather" % world if wl["shard"] == "head"
+                                       else "sequence shard x%d" % world) if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2: %.1f GB of K/V read per step" % (ab_job["decode"] * L / 1e9),
+                       "pages_per_split": pool.pages_per_split(Bl, max_len),
+                       "context_tokens": int((ctx_all + 1).sum())},
+            "hbm_gbs": job_gbs / world,
+            "hbm_frac_of_peak": job_gbs / world / peak,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "vk_decode (decode + merge)",
+                         "peak_source": peak_kind, "launch_ms": dec_avg_ms,
+                         "algorithmic_bytes_per_launch": ab_local["decode"]},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world, gathered, comm):
+    """Same step through the public API, inputs in pinned host memory: each
+    layer's q/k/v is copied host->device on a copy stream (overlapping the
+    previous layer's kernels) and its output device->host."""
+    import torch
+    import torch.distributed as dist
+    g = torch.Generator()
+    g.manual_seed(77)
+    hq = (torch.randn(L, Bl, hq_l, D, generator=g) * 0.5).half().pin_memory()
+    hk = (torch.randn(L, Bl, 1, hkv_l, D, generator=g) * 0.5).half().pin_memory()
+    hv = (torch.randn(L, Bl, 1, hkv_l, D, generator=g) * 0.5).half().pin_memory()
+    gathered_host = gathered is not None
+    out_shape = (L, world, Bl, hq_l, D) if gathered_host else (L, Bl, hq_l, D)
+    hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
+    nbuf = 2
+    dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    dk = [torch.empty(Bl, 1, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    dv = [torch.empty(Bl, 1, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    dout = torch.empty(out_shape[1:] if gathered_host else (L, Bl, hq_l, D), device=dev, dtype=torch.float16) \
+        if not gathered_host else None
+    douts = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
+    compute = torch.cuda.current_stream(dev)
+    h2d_bytes = (hq.numel() + hk.numel() + hv.numel()) * 2
+    d2h_bytes = hout.numel() * 2
+
+    def step():
+        loaded = [None] * nbuf
+        freed = [None] * nbuf
+        outdone = [None] * nbuf
+
+        def load(l):
+            s = l % nbuf
+            with torch.cuda.stream(h2d):
+                if freed[s] is not None:
+                    h2d.wait_event(freed[s])
+                dq[s].copy_(hq[l], non_blocking=True)
+                dk[s].copy_(hk[l], non_blocking=True)
+                dv[s].copy_(hv[l], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                loaded[s] = e
+
+        load(0)
+        for l in range(L):
+            s = l % nbuf
+            if l + 1 < L:
+                load(l + 1)
+            compute.wait_event(loaded[s])
+            if outdone[s] is not None:
+                compute.wait_event(outdone[s])
+            pool.append(l, dk[s], dv[s], bt_d, pos_d)
+            pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
+            fe = torch.cuda.Event()
+            fe.record(compute)
+            freed[s] = fe
+            if gathered_host:
+                comm.wait_event(fe)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(gathered[l].view(-1), douts[s].view(-1))
+                    ge = torch.cuda.Event()
+                    ge.record(comm)
+                d2h.wait_event(ge)
+                src = gathered[l]
+            else:
+                d2h.wait_event(fe)
+                src = douts[s]
+            with torch.cuda.stream(d2h):
+                hout[l].copy_(src, non_blocking=True)
+                od = torch.cuda.Event()
+                od.record(d2h)
+                outdone[s] = od
+        compute.wait_stream(d2h)
+        compute.wait_stream(h2d)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(compute)
+    for _ in range(args.steps):
+        step()
+    t1.record(compute)
+    barrier()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"ms_step": ms / args.steps, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_bytes),
+            "d2h_bytes_per_step": int(d2h_bytes),
+            "path": "PagedKVPool.append/decode (C ABI) with pinned host inputs/outputs, H2D/D2H inside the "
+                    "timed region on copy streams"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,229 @@
+/*
+ * vk_paged_kv.h — C ABI of the B200 paged KV-cache subsystem for VULCAN.
+ *
+ * One shared library (libvulcan_kv.so) exports every function declared here.
+ * Signatures use plain pointers, integers and sizes only, so any FFI (ctypes,
+ * cgo, JNI, N-API) can bind them.  Streams are passed as `void*` holding a
+ * cudaStream_t (NULL = the legacy default stream).  Every device-side entry
+ * point is asynchronous on the given stream and performs no implicit device
+ * synchronisation; functions that must read device state say so.
+ *
+ * Memory layout of a KV pool (fp16, page-major):
+ *
+ *   page p, layer l, kv head h, K-or-V kv, slot s, element d lives at byte
+ *     base + p*page_bytes + l*layer_bytes + h*head_bytes
+ *          + kv*(page_tokens*head_dim*2) + (s*head_dim + d)*2
+ *   head_bytes  = 2 * page_tokens * head_dim * 2      (K block then V block)
+ *   layer_bytes = num_kv_heads * head_bytes
+ *   page_bytes  = num_layers * layer_bytes
+ *
+ * A physical page therefore holds `page_tokens` tokens of every layer, one
+ * block-table entry addresses all layers, and a page is one contiguous byte
+ * range (swap and copy move whole pages with single copies).
+ *
+ * Error convention: every function returns a vk_status (VK_OK = 0) and never
+ * exits the process; vk_last_error_string() describes the last failure on the
+ * calling thread.  Kernels that find a bad block-table entry, position or
+ * sequence length skip the access and record a bit in the pool's device error
+ * word; vk_pool_check() reads and clears it.
+ */
+#ifndef VK_PAGED_KV_H
+#define VK_PAGED_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct vk_pool vk_pool;
+
+typedef enum vk_status {
+    VK_OK = 0,
+    VK_INVALID_ARG = 1,      /* bad argument detected on the host              */
+    VK_OUT_OF_PAGES = 2,     /* allocation could not be satisfied              */
+    VK_CUDA_ERROR = 3,       /* a CUDA runtime call failed                     */
+    VK_TIMEOUT = 4,          /* a bounded device-side wait gave up             */
+    VK_BAD_BLOCK_TABLE = 5,  /* a kernel met an out-of-range page/position     */
+    VK_NOT_FOUND = 6,        /* no such page / nothing swapped for this id     */
+    VK_UNSUPPORTED = 7       /* shape or mode the library does not implement   */
+} vk_status;
+
+/* Device error-word bits reported by vk_pool_check(). */
+#define VK_ERR_PAGE_ID      0x1  /* block-table entry outside [0, num_pages)     */
+#define VK_ERR_TABLE_INDEX  0x2  /* position beyond the block table's capacity   */
+#define VK_ERR_SEQ_LEN      0x4  /* sequence length < 0 or beyond capacity       */
+#define VK_ERR_TIMEOUT      0x8  /* bounded mbarrier wait expired                */
+
+typedef struct vk_pool_cfg {
+    int32_t  num_layers;     /* L                                                */
+    int32_t  num_kv_heads;   /* KV heads held by this pool (this GPU's shard)    */
+    int32_t  head_dim;       /* D: 64, 128 or 256 for attention entry points     */
+    int32_t  page_tokens;    /* tokens per page: 16 for attention entry points   */
+    int32_t  num_pages;      /* physical pages                                   */
+    int32_t  device;         /* CUDA device ordinal                              */
+    uint64_t page_bytes;     /* 0: derived from the KV shape above.  Non-zero:   */
+                             /* a raw byte-page pool (allocator, copy and swap   */
+                             /* only), the MemoryManager(page_size, max_pages)   */
+                             /* form; the KV shape fields are then ignored.      */
+} vk_pool_cfg;
+
+/* ---- pool lifetime --------------------------------------------------------
+ * Replaces KVCache::KVCache / ~KVCache (src/kv_cache.cpp:23-53) and
+ * MemoryManager::MemoryManager / ~MemoryManager (cuda/memory.cu:73-125):
+ * one device allocation carved into fixed-size pages, zero-filled. */
+vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool);
+
+/* As vk_pool_create, but the pool lives in caller-owned device memory
+ * (`bytes` >= num_pages*page_bytes, 256-byte aligned); the library neither
+ * frees nor zero-fills it. */
+vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t bytes,
+                            vk_pool** out_pool);
+
+vk_status vk_pool_destroy(vk_pool* pool);
+
+/* Base device pointer, bytes per page and page count of the pool. */
+void*    vk_pool_base(const vk_pool* pool);
+uint64_t vk_pool_page_bytes(const vk_pool* pool);
+int32_t  vk_pool_num_pages(const vk_pool* pool);
+
+/* Reads (synchronously) and clears the pool's device error word.
+ * VK_OK when it was zero, VK_BAD_BLOCK_TABLE or VK_TIMEOUT otherwise. */
+vk_status vk_pool_check(vk_pool* pool, uint32_t* out_bits);
+
+/* ---- page allocator (host side, not thread-safe, like the reference) ------
+ * vk_alloc_pages replaces MemoryManager::allocate_block (cuda/memory.cu:127-135):
+ * lowest free id first.  All-or-nothing: on VK_OUT_OF_PAGES no page is taken
+ * and every out_ids[i] is set to -1 (the reference's -1 on exhaustion). */
+vk_status vk_alloc_pages(vk_pool* pool, int32_t n, int32_t* out_ids);
+
+/* MemoryManager::free_block (cuda/memory.cu:137-143): ids outside the pool or
+ * already free are ignored; any host swap copy recorded for the id is dropped. */
+vk_status vk_free_pages(vk_pool* pool, const int32_t* ids, int32_t n);
+
+/* MemoryManager::get_block_ptr (cuda/memory.cu:145-150): NULL on a bad id. */
+void* vk_page_ptr(const vk_pool* pool, int32_t id);
+
+/* MemoryManager::blocks_in_use / blocks_available / total_allocated_bytes
+ * (cuda/memory.cu:193-207), O(1). */
+int32_t  vk_pages_in_use(const vk_pool* pool);
+int32_t  vk_pages_available(const vk_pool* pool);
+uint64_t vk_allocated_bytes(const vk_pool* pool);
+/* 1 if the id is allocated, 0 if free, -1 if outside the pool. */
+int32_t  vk_page_in_use(const vk_pool* pool, int32_t id);
+
+/* ---- K1: append ------------------------------------------------------------
+ * Replaces KVCache::append (src/kv_cache.cpp:84-128).  Token t of sequence b
+ * (position positions[b]+t) is written for every KV head to page
+ * block_tables[b*bt_stride + pos/page_tokens], slot pos%page_tokens.
+ * k_new, v_new: [batch, tokens, num_kv_heads, head_dim] fp16 device arrays
+ * (token-major with heads interleaved, the reference's [T, Hkv*D]).
+ * block_tables: int32 [batch, bt_stride]; positions: int32 [batch]. */
+vk_status vk_append(vk_pool* pool, int32_t layer, const void* k_new, const void* v_new,
+                    const int32_t* block_tables, int32_t bt_stride,
+                    const int32_t* positions, int32_t batch, int32_t tokens,
+                    void* stream);
+
+/* As vk_append with fp32 inputs rounded to fp16 (round-to-nearest-even), the
+ * element type of the reference's KVCache::append(const float*, ...). */
+vk_status vk_append_f32(vk_pool* pool, int32_t layer, const float* k_new, const float* v_new,
+                        const int32_t* block_tables, int32_t bt_stride,
+                        const int32_t* positions, int32_t batch, int32_t tokens,
+                        void* stream);
+
+/* ---- K2: paged GQA decode (split-K + merge) --------------------------------
+ * Replaces the decode use of launch_attention (cuda/attention.cu:38-131 as
+ * called per head from src/transformer.cpp:157-189).  For sequence b and query
+ * head h (KV head h / (num_q_heads/num_kv_heads)) it attends the first
+ * seq_lens[b] cached tokens:
+ *   out[b,h,:] = softmax_j(scale * q[b,h,:] . K_j) @ V
+ * q, out: [batch, num_q_heads, head_dim] fp16.  seq_lens: int32 [batch] device
+ * array (a length of 0 yields zeros).  max_seq_len (host) bounds every
+ * seq_lens[b] and sizes the split-K schedule and workspace.
+ * scale <= 0 selects 1/sqrt(head_dim), the reference's scale.
+ * workspace: device scratch of at least vk_decode_workspace_size() bytes. */
+size_t vk_decode_workspace_size(const vk_pool* pool, int32_t batch, int32_t num_q_heads,
+                                int32_t max_seq_len);
+
+vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
+                    const int32_t* block_tables, int32_t bt_stride,
+                    const int32_t* seq_lens, int32_t batch, int32_t num_q_heads,
+                    int32_t max_seq_len, float scale,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Pages per split-K chunk that vk_decode will use for this shape (0 if the
+ * shape is invalid); vk_set_decode_split overrides it for the pool (0 = auto). */
+int32_t   vk_decode_pages_per_split(const vk_pool* pool, int32_t batch, int32_t max_seq_len);
+vk_status vk_set_decode_split(vk_pool* pool, int32_t pages_per_split);
+
+/* ---- K3: chunked prefill -------------------------------------------------
+ * The prefill use of launch_attention (src/transformer.cpp:136-189 with
+ * num_tokens = chunk, src/engine.cpp:70-101): query token t of sequence b sits
+ * at position positions[b]+t and attends cached keys 0..positions[b]+t
+ * (causal).  The chunk's own K/V must already be appended.
+ * q, out: [batch, tokens, num_q_heads, head_dim] fp16. */
+vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, void* out,
+                     const int32_t* block_tables, int32_t bt_stride,
+                     const int32_t* positions, int32_t batch, int32_t tokens,
+                     int32_t num_q_heads, float scale, void* stream);
+
+/* ---- K4: page copy (fork / compaction; no reference counterpart) -----------
+ * dst_ids[i] <- src_ids[i] byte-exactly, whole pages, every layer.  Both are
+ * int32 device arrays of n ids; no id may appear in both arrays. */
+vk_status vk_copy_pages(vk_pool* pool, const int32_t* src_ids, const int32_t* dst_ids,
+                        int32_t n, void* stream);
+
+/* Rewrites block-table entries through a page-id map: every entry e with
+ * 0 <= e < map_len becomes page_map[e].  block_tables: int32 device array of
+ * `entries` ids; page_map: int32 device array. */
+vk_status vk_remap_block_tables(int32_t* block_tables, int64_t entries,
+                                const int32_t* page_map, int32_t map_len, void* stream);
+
+/* Host-side compaction plan: moves the highest in-use pages into the lowest
+ * free ids so that in-use ids become 0..in_use-1.  Writes up to `cap` (src,
+ * dst) pairs, their count to *out_n, and updates the allocator (dst in use,
+ * src free).  Follow with vk_copy_pages and vk_remap_block_tables. */
+vk_status vk_compact_plan(vk_pool* pool, int32_t* src_ids, int32_t* dst_ids, int32_t cap,
+                          int32_t* out_n);
+
+/* ---- K5: pinned-host swap -------------------------------------------------
+ * MemoryManager::swap_to_cpu (cuda/memory.cu:152-169): copies pages ids[0..n)
+ * into host_buf (page i at host_buf + i*page_bytes; page-locked memory for an
+ * asynchronous copy) on `stream`, then frees the ids.  The ids may be handed
+ * out again at once; work that writes them must be ordered after `stream`. */
+vk_status vk_swap_out(vk_pool* pool, const int32_t* ids, int32_t n, void* host_buf,
+                      void* stream);
+
+/* MemoryManager::swap_to_gpu (cuda/memory.cu:171-191), batched: allocates n
+ * new pages (lowest free ids, written to out_ids) and copies host_buf into them
+ * on `stream`.  The new ids may differ from the swapped-out ones; callers
+ * rewrite their block tables with them. */
+vk_status vk_swap_in(vk_pool* pool, const void* host_buf, int32_t n, int32_t* out_ids,
+                     void* stream);
+
+/* Swap-in into the given ids, which must be free (the reference's same-id
+ * swap_to_gpu).  VK_INVALID_ARG if any id is in use or out of range. */
+vk_status vk_swap_in_to(vk_pool* pool, const void* host_buf, const int32_t* ids, int32_t n,
+                        void* stream);
+
+/* ---- compatibility entry: contiguous fp32 causal attention ----------------
+ * Same contract as vulcan::cuda::launch_attention (cuda/attention.cu:119-131,
+ * include/cuda/kernels.h:99-101): Q, K, V, O are [batch, heads, seq_len,
+ * head_dim] fp32 device arrays; row i attends keys 0..i; scale 1/sqrt(D).
+ * Asynchronous on `stream` (the reference synchronises after each launch). */
+vk_status vk_attention_f32(const float* Q, const float* K, const float* V, float* O,
+                           int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim,
+                           void* stream);
+
+/* ---- diagnostics ----------------------------------------------------------- */
+const char* vk_last_error_string(void);
+const char* vk_status_string(vk_status s);
+/* Library version as major*10000 + minor*100 + patch. */
+int32_t vk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VK_PAGED_KV_H */

@@ -1,0 +1,187 @@
+"""CPU oracle for the paged KV-cache path — TEST INFRASTRUCTURE ONLY.
+
+Loads ``liboracle.so`` (the C restatement in ``vk_oracle.c``) and, when it has
+been built, ``_ref/libvulcan_ref.so`` (the reference's own golden attention and
+library, compiled from its sources).  Only ``tests/``, ``__graft_entry__.smoke``
+and the CPU-baseline leg of ``bench.py`` may import this package; the product
+library never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+_REF = None
+
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_c_int = ctypes.c_int
+
+
+def build(ref: bool = False) -> None:
+    """Compile liboracle.so (and oracle/_ref when ``ref`` is set)."""
+    subprocess.run(["make", "-s", "-C", _HERE, "all"] + (["ref"] if ref else []), check=True)
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        L.or_attention_causal.argtypes = [_f32p, _f32p, _f32p, _f32p] + [_c_int] * 4
+        L.or_attention_causal.restype = None
+        L.or_decode_paged.argtypes = ([_u16p] + [_c_int] * 6 + [_u16p, _f32p, _i32p, _c_int, _i32p]
+                                      + [_c_int, _c_int, ctypes.c_float, _c_int])
+        L.or_decode_paged.restype = _c_int
+        L.or_decode_paged_f64.argtypes = ([_u16p] + [_c_int] * 6 + [_u16p, _f64p, _i32p, _c_int,
+                                          _i32p, _c_int, _c_int, ctypes.c_double])
+        L.or_decode_paged_f64.restype = _c_int
+        L.or_prefill_paged.argtypes = ([_u16p] + [_c_int] * 6 + [_u16p, _f32p, _i32p, _c_int, _i32p]
+                                       + [_c_int, _c_int, _c_int, ctypes.c_float, _c_int])
+        L.or_prefill_paged.restype = _c_int
+        L.or_append_paged.argtypes = ([_u16p] + [_c_int] * 6 + [_u16p, _u16p, _i32p, _c_int, _i32p]
+                                      + [_c_int, _c_int])
+        L.or_append_paged.restype = _c_int
+        L.or_copy_pages.argtypes = [_u8p, ctypes.c_uint64, _c_int, _i32p, _i32p, _c_int]
+        L.or_copy_pages.restype = _c_int
+        L.or_remap_block_tables.argtypes = [_i32p, ctypes.c_int64, _i32p, _c_int]
+        L.or_remap_block_tables.restype = None
+        _LIB = L
+    return _LIB
+
+
+def ref_lib():
+    """The reference's own code compiled from its sources, or None if not built."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(_HERE, "_ref", "libvulcan_ref.so")
+        if not os.path.exists(path):
+            return None
+        R = ctypes.CDLL(path)
+        R.ref_random_floats.argtypes = [_c_int, ctypes.c_float, ctypes.c_float, _c_int, _f32p]
+        R.ref_random_floats.restype = None
+        R.ref_cpu_attention.argtypes = [_f32p, _f32p, _f32p, _f32p] + [_c_int] * 4
+        R.ref_cpu_attention.restype = None
+        _REF = R
+    return _REF
+
+
+# ---------------------------------------------------------------- wrappers
+
+class Geom:
+    """Pool geometry: layers, kv heads, head dim, page tokens, pages."""
+
+    def __init__(self, L, Hkv, D, P, num_pages):
+        self.L, self.Hkv, self.D, self.P, self.num_pages = L, Hkv, D, P, num_pages
+
+    @property
+    def page_elems(self):
+        return self.L * self.Hkv * 2 * self.P * self.D
+
+    def pool_shape(self):
+        return (self.num_pages, self.L, self.Hkv, 2, self.P, self.D)
+
+
+def attention_causal(Q, K, V):
+    """Contiguous [B,H,S,D] fp32 causal attention (cpu_attention restated)."""
+    B, H, S, D = Q.shape
+    O = np.zeros_like(Q, dtype=np.float32)
+    lib().or_attention_causal(np.ascontiguousarray(Q, np.float32), np.ascontiguousarray(K, np.float32),
+                              np.ascontiguousarray(V, np.float32), O, B, H, S, D)
+    return O
+
+
+def decode_paged(pool_u16, g: Geom, layer, q_u16, block_tables, seq_lens, scale=0.0, nthreads=1):
+    B, Hq, D = q_u16.shape
+    out = np.zeros((B, Hq, D), np.float32)
+    rc = lib().or_decode_paged(np.ascontiguousarray(pool_u16).reshape(-1), g.L, g.Hkv, g.D, g.P,
+                               g.num_pages, layer, np.ascontiguousarray(q_u16).reshape(-1), out,
+                               np.ascontiguousarray(block_tables, np.int32).reshape(-1),
+                               block_tables.shape[1], np.ascontiguousarray(seq_lens, np.int32),
+                               B, Hq, float(scale), int(nthreads))
+    if rc != 0:
+        raise ValueError("oracle decode: bad block table")
+    return out
+
+
+def decode_paged_f64(pool_u16, g: Geom, layer, q_u16, block_tables, seq_lens, scale=0.0):
+    B, Hq, D = q_u16.shape
+    out = np.zeros((B, Hq, D), np.float64)
+    rc = lib().or_decode_paged_f64(np.ascontiguousarray(pool_u16).reshape(-1), g.L, g.Hkv, g.D, g.P,
+                                   g.num_pages, layer, np.ascontiguousarray(q_u16).reshape(-1), out,
+                                   np.ascontiguousarray(block_tables, np.int32).reshape(-1),
+                                   block_tables.shape[1], np.ascontiguousarray(seq_lens, np.int32),
+                                   B, Hq, float(scale))
+    if rc != 0:
+        raise ValueError("oracle decode: bad block table")
+    return out
+
+
+def prefill_paged(pool_u16, g: Geom, layer, q_u16, block_tables, positions, scale=0.0, nthreads=1):
+    B, T, Hq, D = q_u16.shape
+    out = np.zeros((B, T, Hq, D), np.float32)
+    rc = lib().or_prefill_paged(np.ascontiguousarray(pool_u16).reshape(-1), g.L, g.Hkv, g.D, g.P,
+                                g.num_pages, layer, np.ascontiguousarray(q_u16).reshape(-1), out,
+                                np.ascontiguousarray(block_tables, np.int32).reshape(-1),
+                                block_tables.shape[1], np.ascontiguousarray(positions, np.int32),
+                                B, T, Hq, float(scale), int(nthreads))
+    if rc != 0:
+        raise ValueError("oracle prefill: bad block table")
+    return out
+
+
+def append_paged(pool_u16, g: Geom, layer, k_u16, v_u16, block_tables, positions):
+    """In-place append into a host pool copy; returns 0 or -1 (bad entry skipped)."""
+    B, T = k_u16.shape[0], k_u16.shape[1]
+    flat = pool_u16.reshape(-1)
+    assert flat.base is pool_u16 or flat is pool_u16 or np.shares_memory(flat, pool_u16)
+    return lib().or_append_paged(flat, g.L, g.Hkv, g.D, g.P, g.num_pages, layer,
+                                 np.ascontiguousarray(k_u16).reshape(-1),
+                                 np.ascontiguousarray(v_u16).reshape(-1),
+                                 np.ascontiguousarray(block_tables, np.int32).reshape(-1),
+                                 block_tables.shape[1], np.ascontiguousarray(positions, np.int32), B, T)
+
+
+def copy_pages(pool_bytes, page_bytes, num_pages, src, dst):
+    flat = pool_bytes.reshape(-1)
+    rc = lib().or_copy_pages(flat, page_bytes, num_pages, np.ascontiguousarray(src, np.int32),
+                             np.ascontiguousarray(dst, np.int32), len(src))
+    if rc != 0:
+        raise ValueError("oracle copy: bad id")
+
+
+def remap_block_tables(bt, page_map):
+    flat = np.ascontiguousarray(bt, np.int32).reshape(-1).copy()
+    lib().or_remap_block_tables(flat, flat.size, np.ascontiguousarray(page_map, np.int32), len(page_map))
+    return flat.reshape(bt.shape)
+
+
+def ref_attention_causal(Q, K, V):
+    """The reference's own cpu_attention (compiled from its test file)."""
+    R = ref_lib()
+    if R is None:
+        raise RuntimeError("oracle/_ref not built")
+    B, H, S, D = Q.shape
+    O = np.zeros((B, H, S, D), np.float32)
+    R.ref_cpu_attention(np.ascontiguousarray(Q, np.float32), np.ascontiguousarray(K, np.float32),
+                        np.ascontiguousarray(V, np.float32), O, B, H, S, D)
+    return O
+
+
+def ref_random_floats(n, lo, hi, seed):
+    R = ref_lib()
+    if R is None:
+        raise RuntimeError("oracle/_ref not built")
+    out = np.zeros(n, np.float32)
+    R.ref_random_floats(n, lo, hi, seed, out)
+    return out

@@ -1,0 +1,177 @@
+// K1 append (block-table scatter of new K/V rows), K4 page copy and the
+// block-table remap kernel.
+//
+// Append restates the row scatter of VULCAN's KVCache::append
+// (src/kv_cache.cpp:94-121) with page indirection: token t of sequence b at
+// pos = positions[b]+t goes to page block_tables[b][pos/16], slot pos%16, for
+// every KV head.  The reference issues 2*Hkv*T blocking cudaMemcpy calls; here
+// one launch moves every row with 16-byte vector loads and stores, one warp per
+// (token, kv head) covering its K row and V row.
+#include "vk_internal.h"
+#include "vk_ptx.cuh"
+
+namespace vk {
+
+struct AppendParams {
+    char* base;
+    const void* k;
+    const void* v;
+    const int32_t* bt;
+    const int32_t* pos;
+    uint32_t* err;
+    uint64_t page_bytes, layer_off, head_bytes;
+    int bt_stride, B, T, Hkv, D, P, num_pages;
+};
+
+template <bool F32>
+__global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.Hkv;
+    if (row >= rows) return;
+    const int h = static_cast<int>(row % p.Hkv);
+    const int64_t bt_idx = row / p.Hkv;  // b*T + t
+    const int t = static_cast<int>(bt_idx % p.T);
+    const int b = static_cast<int>(bt_idx / p.T);
+    const int pos = p.pos[b] + t;
+    if (pos < 0 || pos / p.P >= p.bt_stride) {
+        if (lane == 0) atomicOr(p.err, VK_ERR_TABLE_INDEX);
+        return;
+    }
+    const int32_t page = p.bt[static_cast<int64_t>(b) * p.bt_stride + pos / p.P];
+    if (page < 0 || page >= p.num_pages) {
+        if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
+        return;
+    }
+    char* dst_k = p.base + static_cast<uint64_t>(page) * p.page_bytes + p.layer_off +
+                  static_cast<uint64_t>(h) * p.head_bytes +
+                  static_cast<uint64_t>(pos % p.P) * p.D * 2;
+    char* dst_v = dst_k + static_cast<uint64_t>(p.P) * p.D * 2;
+    const int vec_per_row = p.D / 8;  // 8 fp16 = 16 bytes per vector
+    const int64_t src_elem = row * p.D;
+    for (int i = lane; i < 2 * vec_per_row; i += 32) {
+        const bool is_v = i >= vec_per_row;
+        const int vi = is_v ? i - vec_per_row : i;
+        uint4 val;
+        if constexpr (F32) {
+            const float4* src =
+                reinterpret_cast<const float4*>(static_cast<const float*>(is_v ? p.v : p.k) + src_elem) +
+                2 * vi;
+            const float4 a = __ldg(src), c = __ldg(src + 1);
+            val.x = pack_half2(a.x, a.y);
+            val.y = pack_half2(a.z, a.w);
+            val.z = pack_half2(c.x, c.y);
+            val.w = pack_half2(c.z, c.w);
+        } else {
+            const uint4* src =
+                reinterpret_cast<const uint4*>(static_cast<const __half*>(is_v ? p.v : p.k) + src_elem) + vi;
+            val = __ldg(src);
+        }
+        reinterpret_cast<uint4*>(is_v ? dst_v : dst_k)[vi] = val;
+    }
+}
+
+vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, bool f32,
+                        const int32_t* bt, int bt_stride, const int32_t* pos, int B, int T,
+                        cudaStream_t st) {
+    const int D = pool->cfg.head_dim;
+    const uintptr_t align = f32 ? 32 : 16;
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % align)
+        return fail(VK_INVALID_ARG, "k_new/v_new must be 16-byte aligned (32 for fp32)");
+    AppendParams p;
+    p.base = pool->base;
+    p.k = k;
+    p.v = v;
+    p.bt = bt;
+    p.pos = pos;
+    p.err = pool->d_err;
+    p.page_bytes = pool->page_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->layer_bytes;
+    p.head_bytes = pool->head_bytes;
+    p.bt_stride = bt_stride;
+    p.B = B;
+    p.T = T;
+    p.Hkv = pool->cfg.num_kv_heads;
+    p.D = D;
+    p.P = pool->cfg.page_tokens;
+    p.num_pages = pool->num_pages;
+    const int64_t threads = static_cast<int64_t>(B) * T * p.Hkv * 32;
+    const int64_t blocks = (threads + 255) / 256;
+    if (blocks > 0x7fffffff) return fail(VK_INVALID_ARG, "append too large for one launch");
+    if (f32)
+        append_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+    else
+        append_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "append_kernel launch");
+}
+
+// ---------------------------------------------------------------- K4 copy
+
+constexpr int kCopyThreads = 512;
+constexpr int kCopyUnroll = 4;
+constexpr uint64_t kCopyChunk = static_cast<uint64_t>(kCopyThreads) * kCopyUnroll * 16;  // 32 KiB
+
+// grid.x = chunks per page, grid.y = page pairs.  Each CTA moves one 32 KiB
+// chunk of one page with 16-byte loads issued ahead of the stores.
+__global__ void __launch_bounds__(kCopyThreads) copy_pages_kernel(char* base, uint64_t page_bytes,
+                                                                  const int32_t* src,
+                                                                  const int32_t* dst, int num_pages,
+                                                                  uint32_t* err) {
+    const int pair = blockIdx.y;
+    const int32_t s = src[pair], d = dst[pair];
+    if (s < 0 || s >= num_pages || d < 0 || d >= num_pages) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, VK_ERR_PAGE_ID);
+        return;
+    }
+    const uint64_t off = static_cast<uint64_t>(blockIdx.x) * kCopyChunk;
+    const uint4* sp = reinterpret_cast<const uint4*>(base + static_cast<uint64_t>(s) * page_bytes + off);
+    uint4* dp = reinterpret_cast<uint4*>(base + static_cast<uint64_t>(d) * page_bytes + off);
+    const uint64_t left = page_bytes - off;
+    const int nvec = static_cast<int>((left < kCopyChunk ? left : kCopyChunk) / 16);
+    uint4 r[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+        const int i = threadIdx.x + u * kCopyThreads;
+        if (i < nvec) r[u] = __ldcs(sp + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+        const int i = threadIdx.x + u * kCopyThreads;
+        if (i < nvec) __stcs(dp + i, r[u]);
+    }
+}
+
+vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* dst, int n,
+                            cudaStream_t st) {
+    if (pool->page_bytes % 16) return fail(VK_UNSUPPORTED, "copy needs page_bytes % 16 == 0");
+    if (n > 65535) return fail(VK_INVALID_ARG, "copy_pages: at most 65535 pages per call");
+    const uint64_t chunks = (pool->page_bytes + kCopyChunk - 1) / kCopyChunk;
+    if (chunks > 0x7fffffff) return fail(VK_INVALID_ARG, "page too large");
+    dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n));
+    copy_pages_kernel<<<grid, kCopyThreads, 0, st>>>(pool->base, pool->page_bytes, src, dst,
+                                                     pool->num_pages, pool->d_err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "copy_pages_kernel launch");
+}
+
+// ---------------------------------------------------------------- remap
+
+__global__ void remap_kernel(int32_t* bt, int64_t entries, const int32_t* map, int map_len) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < entries;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int32_t e = bt[i];
+        if (e >= 0 && e < map_len) bt[i] = map[e];
+    }
+}
+
+vk_status launch_remap(int32_t* bt, int64_t entries, const int32_t* map, int map_len,
+                       cudaStream_t st) {
+    int64_t blocks = (entries + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    remap_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(bt, entries, map, map_len);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "remap_kernel launch");
+}
+
+}  // namespace vk

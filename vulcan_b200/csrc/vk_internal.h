@@ -1,0 +1,85 @@
+// Internal definitions shared by the translation units of libvulcan_kv.so.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "vk_paged_kv.h"
+
+namespace vk {
+
+constexpr int kPageTokens = 16;     // tokens per page for the attention kernels
+constexpr int kNumSmsDefault = 148;
+
+struct Allocator {
+    // free_bits[w] bit i set <=> page 64*w+i is free.  `hint` is a lower bound
+    // on the first word that may hold a free bit, so lowest-id allocation is
+    // amortised O(1) and every id order matches a first-fit scan.
+    std::vector<uint64_t> free_bits;
+    std::vector<uint8_t> swapped;  // an id whose contents were swapped out
+    size_t hint = 0;
+    int32_t num_pages = 0;
+    int32_t used = 0;
+
+    void reset(int32_t n);
+    int32_t take_lowest();           // -1 when full
+    bool is_used(int32_t id) const;
+    void set_used(int32_t id);
+    void set_free(int32_t id);
+};
+
+}  // namespace vk
+
+struct vk_pool {
+    vk_pool_cfg cfg{};
+    bool kv = false;           // KV geometry present (attention entry points allowed)
+    bool owns_mem = false;
+    int device = 0;
+    char* base = nullptr;
+    uint64_t page_bytes = 0;
+    uint64_t layer_bytes = 0;
+    uint64_t head_bytes = 0;
+    int32_t num_pages = 0;
+    uint32_t* d_err = nullptr;  // device error word (VK_ERR_* bits)
+    alignas(64) CUtensorMap tmap;  // 2-D view: rows of head_dim fp16 over the whole pool
+    bool tmap_ok = false;
+    int32_t split_override = 0;
+    int32_t num_sms = vk::kNumSmsDefault;
+    vk::Allocator alloc;
+};
+
+namespace vk {
+
+// Error reporting (thread-local last error string).
+vk_status fail(vk_status s, const std::string& msg);
+vk_status cuda_fail(cudaError_t e, const char* what);
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Device guard: makes the pool's device current for the scope.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+        else prev = -1;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// Kernel launchers (defined in the .cu files).
+vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, bool f32,
+                        const int32_t* bt, int bt_stride, const int32_t* pos, int B, int T,
+                        cudaStream_t st);
+vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* dst, int n,
+                            cudaStream_t st);
+vk_status launch_remap(int32_t* bt, int64_t entries, const int32_t* map, int map_len,
+                       cudaStream_t st);
+int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len);
+
+}  // namespace vk

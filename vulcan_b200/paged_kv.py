@@ -1,0 +1,400 @@
+"""Python mirror of VULCAN's KV-cache interfaces over the B200 C ABI.
+
+Three layers, all calling libvulcan_kv.so (no CPU path):
+
+* ``PagedKVPool`` — the batched paged API: page allocator, append (K1),
+  paged GQA decode with split-K (K2), chunked prefill (K3), page copy (K4) and
+  pinned-host swap (K5).  Tensors are torch tensors; work is enqueued on the
+  current CUDA stream.
+* ``MemoryManager`` — the reference's ``vulcan::cuda::MemoryManager``
+  (include/cuda/memory.h:87-128): byte pages, ``allocate_block`` returning -1
+  when full, ``get_block_ptr`` returning None for a bad id, ``swap_to_cpu`` /
+  ``swap_to_gpu`` returning False on failure.
+* ``KVCache`` — the reference's ``vulcan::KVCache`` (include/vulcan/kv_cache.h:
+  34-92) for one sequence: ``append(layer, k_new, v_new, start_pos,
+  num_tokens)`` with fp32 inputs, length bookkeeping, ``memory_usage``.  Pages
+  are fp16 and taken on demand.
+
+``launch_attention`` mirrors ``vulcan::cuda::launch_attention``
+(include/cuda/kernels.h:99-101) on contiguous fp32 tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import sys
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import VKError, check
+
+PAGE_TOKENS = 16
+
+
+def _stream(stream=None) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _i32_array(ids: Sequence[int]):
+    arr = (ctypes.c_int32 * max(1, len(ids)))(*ids)
+    return arr
+
+
+def _need(t: torch.Tensor, dtype, name: str, device=True):
+    if t.dtype != dtype:
+        raise TypeError("%s must be %s, got %s" % (name, dtype, t.dtype))
+    if device and not t.is_cuda:
+        raise TypeError("%s must be a CUDA tensor" % name)
+    if not t.is_contiguous():
+        raise ValueError("%s must be contiguous" % name)
+
+
+class PagedKVPool:
+    """A paged fp16 KV pool for ``num_layers`` layers and ``num_kv_heads`` heads.
+
+    Memory layout per page (see include/vk_paged_kv.h):
+    ``[num_layers, num_kv_heads, 2 (K,V), page_tokens, head_dim]`` fp16.  The
+    pool storage is a torch allocation handed to the library
+    (``vk_pool_create_in``) unless ``own_memory`` is set.
+    """
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_pages: int,
+                 page_tokens: int = PAGE_TOKENS, device=None, own_memory: bool = False,
+                 page_bytes: int = 0, zero: bool = True):
+        self._lib = _lib.load()
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                           (device.index if isinstance(device, torch.device) else int(device)))
+        self.device = dev
+        self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
+        self.page_tokens, self.num_pages = page_tokens, num_pages
+        cfg = _lib.VkPoolCfg(num_layers, num_kv_heads, head_dim, page_tokens, num_pages, dev.index,
+                             page_bytes)
+        self.kv = page_bytes == 0
+        self.page_bytes = page_bytes if page_bytes else (
+            num_layers * num_kv_heads * 2 * page_tokens * head_dim * 2)
+        handle = ctypes.c_void_p()
+        self.storage = None
+        with torch.cuda.device(dev):
+            if own_memory:
+                check(self._lib.vk_pool_create(ctypes.byref(cfg), ctypes.byref(handle)), "vk_pool_create")
+            else:
+                nbytes = self.page_bytes * num_pages
+                self.storage = (torch.zeros if zero else torch.empty)(nbytes, dtype=torch.uint8, device=dev)
+                check(self._lib.vk_pool_create_in(ctypes.byref(cfg), _ptr(self.storage), nbytes,
+                                                  ctypes.byref(handle)), "vk_pool_create_in")
+        self.handle = handle
+        self._ws = None
+
+    # ------------------------------------------------------------------ views
+    def kv_view(self) -> torch.Tensor:
+        """fp16 view [num_pages, L, Hkv, 2, page_tokens, head_dim] of the pool."""
+        if self.storage is None or not self.kv:
+            raise RuntimeError("kv_view needs a torch-backed KV pool")
+        return self.storage.view(torch.float16).view(self.num_pages, self.num_layers, self.num_kv_heads,
+                                                     2, self.page_tokens, self.head_dim)
+
+    @property
+    def base_ptr(self) -> int:
+        return self._lib.vk_pool_base(self.handle) or 0
+
+    # -------------------------------------------------------------- allocator
+    def alloc(self, n: int) -> List[int]:
+        ids = (ctypes.c_int32 * max(1, n))()
+        check(self._lib.vk_alloc_pages(self.handle, n, ids), "vk_alloc_pages")
+        return list(ids[:n])
+
+    def free(self, ids: Sequence[int]) -> None:
+        check(self._lib.vk_free_pages(self.handle, _i32_array(ids), len(ids)), "vk_free_pages")
+
+    def page_ptr(self, page_id: int) -> Optional[int]:
+        return self._lib.vk_page_ptr(self.handle, page_id)
+
+    def pages_in_use(self) -> int:
+        return self._lib.vk_pages_in_use(self.handle)
+
+    def pages_available(self) -> int:
+        return self._lib.vk_pages_available(self.handle)
+
+    def allocated_bytes(self) -> int:
+        return self._lib.vk_allocated_bytes(self.handle)
+
+    def page_in_use(self, page_id: int) -> int:
+        return self._lib.vk_page_in_use(self.handle, page_id)
+
+    def check(self) -> int:
+        """Synchronises, reads and clears the device error word; raises on error."""
+        bits = ctypes.c_uint32(0)
+        st = self._lib.vk_pool_check(self.handle, ctypes.byref(bits))
+        if st != _lib.VK_OK:
+            raise VKError(st, "device error bits 0x%x" % bits.value)
+        return bits.value
+
+    def error_bits(self) -> int:
+        """Like check() but returns the bits instead of raising."""
+        bits = ctypes.c_uint32(0)
+        self._lib.vk_pool_check(self.handle, ctypes.byref(bits))
+        return bits.value
+
+    # ----------------------------------------------------------------- kernels
+    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor, block_tables: torch.Tensor,
+               positions: torch.Tensor, stream=None) -> None:
+        """k_new/v_new: [B, T, Hkv, D] fp16 (or fp32); block_tables [B, W] int32; positions [B] int32."""
+        B, T = k_new.shape[0], k_new.shape[1]
+        _need(block_tables, torch.int32, "block_tables")
+        _need(positions, torch.int32, "positions")
+        if k_new.dtype == torch.float32:
+            fn = self._lib.vk_append_f32
+        else:
+            _need(k_new, torch.float16, "k_new")
+            fn = self._lib.vk_append
+        _need(v_new, k_new.dtype, "v_new")
+        check(fn(self.handle, layer, _ptr(k_new), _ptr(v_new), _ptr(block_tables), block_tables.shape[1],
+                 _ptr(positions), B, T, _stream(stream)), "vk_append")
+
+    def workspace_size(self, batch: int, num_q_heads: int, max_seq_len: int) -> int:
+        return self._lib.vk_decode_workspace_size(self.handle, batch, num_q_heads, max_seq_len)
+
+    def pages_per_split(self, batch: int, max_seq_len: int) -> int:
+        return self._lib.vk_decode_pages_per_split(self.handle, batch, max_seq_len)
+
+    def set_split(self, pages_per_split: int) -> None:
+        check(self._lib.vk_set_decode_split(self.handle, pages_per_split), "vk_set_decode_split")
+
+    def workspace(self, batch: int, num_q_heads: int, max_seq_len: int) -> Optional[torch.Tensor]:
+        need = self.workspace_size(batch, num_q_heads, max_seq_len)
+        if need == 0:
+            return None
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def decode(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor, seq_lens: torch.Tensor,
+               max_seq_len: int, out: Optional[torch.Tensor] = None, scale: float = 0.0,
+               workspace: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """q: [B, Hq, D] fp16; seq_lens [B] int32 (tokens to attend); returns [B, Hq, D] fp16."""
+        _need(q, torch.float16, "q")
+        _need(block_tables, torch.int32, "block_tables")
+        _need(seq_lens, torch.int32, "seq_lens")
+        B, Hq, _ = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        if workspace is None:
+            workspace = self.workspace(B, Hq, max_seq_len)
+        ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(self._lib.vk_decode(self.handle, layer, _ptr(q), _ptr(out), _ptr(block_tables),
+                                  block_tables.shape[1], _ptr(seq_lens), B, Hq, max_seq_len, float(scale),
+                                  _ptr(workspace), ws_bytes, _stream(stream)), "vk_decode")
+        return out
+
+    def prefill(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor, positions: torch.Tensor,
+                out: Optional[torch.Tensor] = None, scale: float = 0.0, stream=None) -> torch.Tensor:
+        """q: [B, T, Hq, D] fp16; positions [B] int32 (chunk start); returns [B, T, Hq, D] fp16."""
+        _need(q, torch.float16, "q")
+        _need(block_tables, torch.int32, "block_tables")
+        _need(positions, torch.int32, "positions")
+        B, T, Hq, _ = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        check(self._lib.vk_prefill(self.handle, layer, _ptr(q), _ptr(out), _ptr(block_tables),
+                                   block_tables.shape[1], _ptr(positions), B, T, Hq, float(scale),
+                                   _stream(stream)), "vk_prefill")
+        return out
+
+    def copy_pages(self, src_ids: torch.Tensor, dst_ids: torch.Tensor, stream=None) -> None:
+        _need(src_ids, torch.int32, "src_ids")
+        _need(dst_ids, torch.int32, "dst_ids")
+        check(self._lib.vk_copy_pages(self.handle, _ptr(src_ids), _ptr(dst_ids), src_ids.numel(),
+                                      _stream(stream)), "vk_copy_pages")
+
+    def compact_plan(self, cap: Optional[int] = None):
+        cap = self.num_pages if cap is None else cap
+        src = (ctypes.c_int32 * max(1, cap))()
+        dst = (ctypes.c_int32 * max(1, cap))()
+        n = ctypes.c_int32(0)
+        check(self._lib.vk_compact_plan(self.handle, src, dst, cap, ctypes.byref(n)), "vk_compact_plan")
+        return list(src[:n.value]), list(dst[:n.value])
+
+    def swap_out(self, ids: Sequence[int], host: torch.Tensor, stream=None) -> None:
+        """Copies pages ``ids`` into pinned ``host`` (uint8, >= len(ids)*page_bytes) and frees them."""
+        check(self._lib.vk_swap_out(self.handle, _i32_array(ids), len(ids), _ptr(host), _stream(stream)),
+              "vk_swap_out")
+
+    def swap_in(self, host: torch.Tensor, n: int, stream=None) -> List[int]:
+        ids = (ctypes.c_int32 * max(1, n))()
+        check(self._lib.vk_swap_in(self.handle, _ptr(host), n, ids, _stream(stream)), "vk_swap_in")
+        return list(ids[:n])
+
+    def swap_in_to(self, host: torch.Tensor, ids: Sequence[int], stream=None) -> None:
+        check(self._lib.vk_swap_in_to(self.handle, _ptr(host), _i32_array(ids), len(ids), _stream(stream)),
+              "vk_swap_in_to")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self._lib.vk_pool_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+        self.storage = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def remap_block_tables(block_tables: torch.Tensor, page_map: torch.Tensor, stream=None) -> None:
+    _need(block_tables, torch.int32, "block_tables")
+    _need(page_map, torch.int32, "page_map")
+    check(_lib.load().vk_remap_block_tables(_ptr(block_tables), block_tables.numel(), _ptr(page_map),
+                                            page_map.numel(), _stream(stream)), "vk_remap_block_tables")
+
+
+def launch_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, O: torch.Tensor, batch: int,
+                     heads: int, seq_len: int, head_dim: int, stream=None) -> None:
+    """vulcan::cuda::launch_attention on contiguous fp32 [B, H, S, D] tensors."""
+    for t, n in ((Q, "Q"), (K, "K"), (V, "V"), (O, "O")):
+        _need(t, torch.float32, n)
+    check(_lib.load().vk_attention_f32(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), batch, heads, seq_len, head_dim,
+                                       _stream(stream)), "vk_attention_f32")
+
+
+class MemoryManager:
+    """vulcan::cuda::MemoryManager(page_size, max_pages) over a raw byte-page pool."""
+
+    DEFAULT_PAGE_SIZE = 16 * 1024
+
+    def __init__(self, page_size: int = DEFAULT_PAGE_SIZE, max_pages: int = 1024, device=None):
+        self.page_size = page_size
+        self.max_pages = max_pages
+        self._pool = PagedKVPool(0, 0, 0, max_pages, page_tokens=0, device=device, own_memory=True,
+                                 page_bytes=page_size)
+        self._swap = {}  # id -> pinned host tensor
+
+    def allocate_block(self) -> int:
+        try:
+            return self._pool.alloc(1)[0]
+        except VKError as e:
+            if e.status == _lib.VK_OUT_OF_PAGES:
+                return -1
+            raise
+
+    def free_block(self, block_id: int) -> None:
+        self._pool.free([block_id])
+        self._swap.pop(block_id, None)
+
+    def get_block_ptr(self, block_id: int) -> Optional[int]:
+        return self._pool.page_ptr(block_id)
+
+    def swap_to_cpu(self, block_id: int) -> bool:
+        if not (0 <= block_id < self.max_pages) or self._pool.page_in_use(block_id) != 1:
+            return False
+        host = torch.empty(self.page_size, dtype=torch.uint8, pin_memory=True)
+        st = torch.cuda.current_stream(self._pool.device)
+        if self._pool._lib.vk_swap_out(self._pool.handle, _i32_array([block_id]), 1, _ptr(host),
+                                       _stream(st)) != _lib.VK_OK:
+            return False
+        st.synchronize()
+        self._swap[block_id] = host
+        return True
+
+    def swap_to_gpu(self, block_id: int) -> bool:
+        if not (0 <= block_id < self.max_pages) or block_id not in self._swap:
+            return False
+        st = torch.cuda.current_stream(self._pool.device)
+        if self._pool._lib.vk_swap_in_to(self._pool.handle, _ptr(self._swap[block_id]),
+                                         _i32_array([block_id]), 1, _stream(st)) != _lib.VK_OK:
+            return False
+        st.synchronize()
+        del self._swap[block_id]
+        return True
+
+    def blocks_in_use(self) -> int:
+        return self._pool.pages_in_use()
+
+    def blocks_available(self) -> int:
+        return self._pool.pages_available()
+
+    def total_allocated_bytes(self) -> int:
+        return self._pool.allocated_bytes()
+
+
+class KVCache:
+    """vulcan::KVCache(num_kv_heads, max_seq_len, head_dim, num_layers) for one
+    sequence on a paged fp16 pool; pages are taken on demand by ``append``."""
+
+    def __init__(self, num_kv_heads: int, max_seq_len: int, head_dim: int, num_layers: int, device=None):
+        self._num_kv_heads, self._max_seq_len = num_kv_heads, max_seq_len
+        self._head_dim, self._num_layers = head_dim, num_layers
+        pages = (max_seq_len + PAGE_TOKENS - 1) // PAGE_TOKENS
+        self.pool = PagedKVPool(num_layers, num_kv_heads, head_dim, pages, device=device)
+        self.block_table = torch.full((1, pages), -1, dtype=torch.int32, device=self.pool.device)
+        self._pages: List[int] = []
+        self._current_len = 0
+
+    def _ensure_pages(self, end: int) -> None:
+        need = (end + PAGE_TOKENS - 1) // PAGE_TOKENS
+        if need > len(self._pages):
+            new = self.pool.alloc(need - len(self._pages))
+            self.block_table[0, len(self._pages):need] = torch.tensor(new, dtype=torch.int32)
+            self._pages += new
+
+    def append(self, layer: int, k_new: torch.Tensor, v_new: torch.Tensor, start_pos: int,
+               num_tokens: int) -> None:
+        """k_new/v_new: [num_tokens, num_kv_heads*head_dim] (fp32 or fp16) CUDA tensors."""
+        if layer < 0 or layer >= self._num_layers:
+            return  # the reference returns silently (src/kv_cache.cpp:86)
+        if start_pos + num_tokens > self._max_seq_len:
+            print("[VULCAN] KV Cache overflow: pos=%d + tokens=%d > max_seq=%d"
+                  % (start_pos, num_tokens, self._max_seq_len), file=sys.stderr)
+            return
+        self._ensure_pages(start_pos + num_tokens)
+        k = k_new.reshape(1, num_tokens, self._num_kv_heads, self._head_dim)
+        v = v_new.reshape(1, num_tokens, self._num_kv_heads, self._head_dim)
+        pos = torch.tensor([start_pos], dtype=torch.int32, device=self.pool.device)
+        self.pool.append(layer, k, v, self.block_table, pos)
+        self._current_len = max(self._current_len, start_pos + num_tokens)
+
+    def get(self, layer: int):
+        """Pool addresses of this layer's K and V blocks of physical page 0; the
+        element at (page, kv head, slot, d) of layer ``layer`` is at
+        ``k + page*page_bytes + head*2*P*D*2 + (slot*D + d)*2`` (V: ``v`` + same)."""
+        if layer < 0 or layer >= self._num_layers:
+            return None, None
+        base = self.pool.base_ptr
+        k = base + layer * self._num_kv_heads * 2 * PAGE_TOKENS * self._head_dim * 2
+        return k, k + PAGE_TOKENS * self._head_dim * 2
+
+    def decode(self, layer: int, q: torch.Tensor, num_q_heads: Optional[int] = None) -> torch.Tensor:
+        """Attention of one query token ([num_q_heads, head_dim] fp16) over the cached tokens."""
+        hq = num_q_heads or q.shape[0]
+        lens = torch.tensor([self._current_len], dtype=torch.int32, device=self.pool.device)
+        return self.pool.decode(layer, q.reshape(1, hq, self._head_dim).contiguous(), self.block_table, lens,
+                                self._max_seq_len)[0]
+
+    def current_length(self) -> int:
+        return self._current_len
+
+    def set_length(self, length: int) -> None:
+        self._current_len = length
+
+    def reset(self) -> None:
+        self._current_len = 0
+
+    def max_seq_len(self) -> int:
+        return self._max_seq_len
+
+    def memory_usage(self) -> int:
+        """Bytes of fp16 storage for max_seq_len tokens: 2*L*Hkv*ceil(S/16)*16*D*2."""
+        pages = (self._max_seq_len + PAGE_TOKENS - 1) // PAGE_TOKENS
+        return 2 * self._num_layers * self._num_kv_heads * pages * PAGE_TOKENS * self._head_dim * 2
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)
