@@ -224,10 +224,19 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pps", type=int, default=0, help="override decode pages per split (0 = auto)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
+    ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     wl = workload(args.config)
+    if args.layers:
+        wl["L"] = args.layers
+        wl["desc"] += " [profiling case: %d layers]" % args.layers
+    if args.batch:
+        wl["B"] = args.batch
+        wl["ctx"] = wl["ctx"][:args.batch]
+        wl["desc"] += " [profiling case: first %d sequences]" % args.batch
     if args.impl == "reference":
         return run_reference_arm(args, wl)
 
