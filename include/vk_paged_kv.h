@@ -216,6 +216,37 @@ vk_status vk_attention_f32(const float* Q, const float* K, const float* V, float
                            int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim,
                            void* stream);
 
+/* ---- decode without any device allocation ---------------------------------
+ * No counterpart in the reference.  Same computation and result as vk_decode
+ * (it runs vk_decode with the same split-K schedule), but the split-K scratch
+ * comes from a fixed array compiled into the library instead of a caller
+ * workspace.  It is meant for callers that cannot allocate device memory: a
+ * host engine or plugin framework that owns all device memory and hands an
+ * operator only its inputs and outputs, a serving loop that must not call
+ * cudaMalloc (which can synchronise the device), or an FFI host (cgo, JNI)
+ * with no CUDA allocator.  The caller still passes q, out, block tables and
+ * lengths.
+ *
+ * Limit: the shape must need at most VK_DECODE_STATIC_SCRATCH_BYTES of scratch
+ * (vk_decode_workspace_size() for the same arguments); larger shapes return
+ * VK_INVALID_ARG with a message, and nothing is launched.  Every GPU that
+ * uses this entry point holds the array until the process exits.
+ *
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  All calls on a device share the one array and it keeps the last
+ * call's contents; nothing in it needs to start at zero, because every split
+ * writes its partial result before the merge reads it.  Calls that overlap on
+ * the GPU (different streams, or concurrent host threads) race on the array:
+ * order them on one stream.  The function never calls cudaMalloc, cudaFree or
+ * any allocating library routine. */
+#define VK_DECODE_STATIC_SCRATCH_BYTES (32u << 20)
+
+vk_status vk_decode_static(vk_pool* pool, int32_t layer, const void* q, void* out,
+                           const int32_t* block_tables, int32_t bt_stride,
+                           const int32_t* seq_lens, int32_t batch, int32_t num_q_heads,
+                           int32_t max_seq_len, float scale, void* stream);
+
 /* ---- diagnostics ----------------------------------------------------------- */
 const char* vk_last_error_string(void);
 const char* vk_status_string(vk_status s);

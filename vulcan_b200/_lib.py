@@ -51,6 +51,7 @@ SIGNATURES = {
     "vk_decode_workspace_size": (c_sz, [vp, c_i32, c_i32, c_i32]),
     "vk_decode": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp, c_sz,
                           vp]),
+    "vk_decode_static": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
     "vk_decode_pages_per_split": (c_i32, [vp, c_i32, c_i32]),
     "vk_set_decode_split": (c_i32, [vp, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
