@@ -223,7 +223,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="planned", choices=["planned", "split"],
+                    help="planned: one persistent launch per layer (append+decode+merge fused); "
+                         "split: vk_append + vk_decode (split grid + merge kernel)")
     ap.add_argument("--pps", type=int, default=0, help="override decode pages per split (0 = auto)")
+    ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
     ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
     args = ap.parse_args()
@@ -301,6 +305,10 @@ def main():
     vn = (torch.randn(L, Bl, 1, hkv_l, D, device=dev, generator=gen) * 0.5).half()
     out = torch.empty(L, Bl, hq_l, D, device=dev, dtype=torch.float16)
     ws = pool.workspace(Bl, hq_l, max_len)
+    lens_host = lens.tolist()
+    kn3 = kn.view(L, Bl, hkv_l, D)
+    vn3 = vn.view(L, Bl, hkv_l, D)
+    plan_ws = torch.empty(pool.plan(lens_host, hq_l).workspace.numel() + 4096, dtype=torch.uint8, device=dev)
     gathered = None
     comm = None
     if world > 1 and wl["shard"] == "head":
@@ -308,32 +316,40 @@ def main():
         comm = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
     merge_launched = 1 if pool.workspace_size(Bl, hq_l, max_len) > 0 else 0
-    launches_per_step = L * (2 + merge_launched)
+    launches_per_step = L * (2 + merge_launched) if args.path == "split" else L
 
-    dec_events = []
+    use_graph = world == 1 and not args.eager
+    plan_keep = {}
 
-    def step(record=False):
-        evs = []
+    def new_plan():
+        """Host plan for this step (every layer shares the lengths), uploaded in stream order."""
+        if args.path == "planned":
+            p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+            p_.upload()
+            plan_keep["plan"] = p_
+
+    def layers(events=None):
+        plan = plan_keep.get("plan")
+        cur = torch.cuda.current_stream(dev)
         for l in range(L):
-            pool.append(l, kn[l], vn[l], bt_d, pos_d)
-            if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record(compute)
-            pool.decode(l, q[l], bt_d, lens_d, max_len, out=out[l], workspace=ws)
-            if record:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record(compute)
-                evs.append((e0, e1))
+            if args.path == "split":
+                pool.append(l, kn[l], vn[l], bt_d, pos_d)
+            if events is not None:
+                events[l][0].record(cur)
+            if args.path == "split":
+                pool.decode(l, q[l], bt_d, lens_d, max_len, out=out[l], workspace=ws)
+            else:
+                plan.run(l, q[l], bt_d, out=out[l], k_new=kn3[l], v_new=vn3[l])
+            if events is not None:
+                events[l][1].record(cur)
             if gathered is not None:
                 ev = torch.cuda.Event()
-                ev.record(compute)
+                ev.record(cur)
                 comm.wait_event(ev)
                 with torch.cuda.stream(comm):
                     dist.all_gather_into_tensor(gathered[l].view(-1), out[l].view(-1))
         if gathered is not None:
-            compute.wait_stream(comm)
-        if record:
-            dec_events.extend(evs)
+            cur.wait_stream(comm)
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -342,8 +358,36 @@ def main():
         torch.cuda.synchronize(dev)
 
     for _ in range(args.warmup):
-        step()
+        new_plan()
+        layers()
     pool.check()  # no device errors during warm-up
+    barrier()
+
+    graph = None
+    if use_graph:
+        # the whole L-layer step as one CUDA graph; timing events are graph nodes
+        layer_events = [(torch.cuda.Event(enable_timing=True, external=True),
+                         torch.cuda.Event(enable_timing=True, external=True)) for _ in range(L)]
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(compute)
+        with torch.cuda.graph(graph, stream=cap):
+            layers(layer_events)
+        compute.wait_stream(cap)
+        new_plan()
+        graph.replay()
+        pool.check()
+
+        def step():
+            new_plan()
+            graph.replay()
+    else:
+        layer_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                        for _ in range(L)]
+
+        def step():
+            new_plan()
+            layers(layer_events)
     barrier()
 
     t_start = torch.cuda.Event(enable_timing=True)
@@ -351,7 +395,7 @@ def main():
     with ClockSampler(local) as clk:
         t_start.record(compute)
         for _ in range(args.steps):
-            step(record=True)
+            step()
         t_end.record(compute)
         barrier()
     ms_total = t_start.elapsed_time(t_end)
@@ -360,8 +404,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
     ms_step = ms_total / args.steps
-    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
-    dec_avg_ms = sum(dec_ms) / len(dec_ms)
+    try:  # per-launch durations of the last timed step
+        dec_ms = [a.elapsed_time(b) for a, b in layer_events]
+        dec_avg_ms = sum(dec_ms) / len(dec_ms)
+        dec_src = "CUDA events around each decode launch of the last timed step"
+    except RuntimeError:
+        dec_avg_ms = ms_step / L
+        dec_src = "step time / layers (events unavailable)"
     clocks = clk.summary()
 
     # --- algorithmic bytes (this rank's share) and roofline of the decode launch
@@ -376,7 +425,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world,
-                      gathered, comm)
+                      gathered, comm, lens_host, plan_ws, use_graph)
         e2e["value"] = B / (e2e.pop("ms_step") * 1e-3)
 
     # --- CPU baseline (rank 0 at N=1 only): oracle port, 1 thread, bounded sample
@@ -402,53 +451,71 @@ def main():
                        "parallelism": ("kv-head shard x%d + NCCL allgather" % world if wl["shard"] == "head"
                                        else "sequence shard x%d" % world) if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: %.1f GB of K/V read per step" % (ab_job["decode"] * L / 1e9),
-                       "pages_per_split": pool.pages_per_split(Bl, max_len),
+                       "decode_path": args.path,
+                       "launch": "CUDA graph of the %d-layer step" % L if use_graph else "eager",
+                       "pages_per_split": pool.pages_per_split(Bl, max_len) if args.path == "split" else None,
+                       "plan_workers": pool.plan(lens_host, hq_l).workers if args.path == "planned" else None,
                        "context_tokens": int((ctx_all + 1).sum())},
             "hbm_gbs": job_gbs / world,
             "hbm_frac_of_peak": job_gbs / world / peak,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "vk_decode (decode + merge)",
-                         "peak_source": peak_kind, "launch_ms": dec_avg_ms,
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": ("vk_decode_run (planned: append + decode + merge in one launch)"
+                                    if args.path == "planned" else "vk_decode (split grid + merge)"),
+                         "peak_source": peak_kind, "launch_ms": dec_avg_ms, "launch_timing": dec_src,
                          "algorithmic_bytes_per_launch": ab_local["decode"]},
             "cpu_baseline": cpu,
             "e2e": e2e,
         }
         print(json.dumps(line), flush=True)
+    del graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world, gathered, comm):
-    """Same step through the public API, inputs in pinned host memory: each
-    layer's q/k/v is copied host->device on a copy stream (overlapping the
-    previous layer's kernels) and its output device->host."""
+def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world, gathered, comm,
+            lens_host, plan_ws, use_graph):
+    """Same step through the public API with host buffers: each layer's q/k/v is
+    copied from pinned host memory to the device on a copy stream (double
+    buffered, overlapping the previous layer's kernel) and each layer's output
+    is copied back to pinned host memory on a second copy stream, all inside
+    the timed region.  At N=1 the step is one CUDA graph."""
     import torch
     import torch.distributed as dist
     g = torch.Generator()
     g.manual_seed(77)
     hq = (torch.randn(L, Bl, hq_l, D, generator=g) * 0.5).half().pin_memory()
-    hk = (torch.randn(L, Bl, 1, hkv_l, D, generator=g) * 0.5).half().pin_memory()
-    hv = (torch.randn(L, Bl, 1, hkv_l, D, generator=g) * 0.5).half().pin_memory()
+    hk = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
+    hv = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
     gathered_host = gathered is not None
     out_shape = (L, world, Bl, hq_l, D) if gathered_host else (L, Bl, hq_l, D)
     hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
     nbuf = 2
     dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    dk = [torch.empty(Bl, 1, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    dv = [torch.empty(Bl, 1, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    dout = torch.empty(out_shape[1:] if gathered_host else (L, Bl, hq_l, D), device=dev, dtype=torch.float16) \
-        if not gathered_host else None
+    dk = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    dv = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
     douts = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
     h2d = torch.cuda.Stream(device=dev)
     d2h = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
     h2d_bytes = (hq.numel() + hk.numel() + hv.numel()) * 2
     d2h_bytes = hout.numel() * 2
+    plan_keep = {}
 
-    def step():
+    def new_plan():
+        if args.path == "planned":
+            p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+            p_.upload()
+            plan_keep["plan"] = p_
+
+    def layers():
+        cur = torch.cuda.current_stream(dev)
+        plan = plan_keep.get("plan")
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
         loaded = [None] * nbuf
         freed = [None] * nbuf
         outdone = [None] * nbuf
@@ -470,13 +537,16 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             s = l % nbuf
             if l + 1 < L:
                 load(l + 1)
-            compute.wait_event(loaded[s])
+            cur.wait_event(loaded[s])
             if outdone[s] is not None:
-                compute.wait_event(outdone[s])
-            pool.append(l, dk[s], dv[s], bt_d, pos_d)
-            pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
+                cur.wait_event(outdone[s])
+            if plan is None:
+                pool.append(l, dk[s].view(Bl, 1, hkv_l, D), dv[s].view(Bl, 1, hkv_l, D), bt_d, pos_d)
+                pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
+            else:
+                plan.run(l, dq[s], bt_d, out=douts[s], k_new=dk[s], v_new=dv[s])
             fe = torch.cuda.Event()
-            fe.record(compute)
+            fe.record(cur)
             freed[s] = fe
             if gathered_host:
                 comm.wait_event(fe)
@@ -494,8 +564,8 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
                 od = torch.cuda.Event()
                 od.record(d2h)
                 outdone[s] = od
-        compute.wait_stream(d2h)
-        compute.wait_stream(h2d)
+        cur.wait_stream(d2h)
+        cur.wait_stream(h2d)
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -504,7 +574,26 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
         torch.cuda.synchronize(dev)
 
     for _ in range(args.warmup):
-        step()
+        new_plan()
+        layers()
+    barrier()
+    graph = None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(compute)
+        with torch.cuda.graph(graph, stream=cap):
+            layers()
+        compute.wait_stream(cap)
+
+        def step():
+            new_plan()
+            graph.replay()
+    else:
+        def step():
+            new_plan()
+            layers()
+    step()
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -518,10 +607,11 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    del graph
     return {"ms_step": ms / args.steps, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h_bytes),
-            "path": "PagedKVPool.append/decode (C ABI) with pinned host inputs/outputs, H2D/D2H inside the "
-                    "timed region on copy streams"}
+            "path": "PagedKVPool / DecodePlan (C ABI) with pinned host q, k, v and outputs; H2D and D2H on "
+                    "copy streams inside the timed region" + ("; CUDA graph per step" if use_graph else "")}
 
 
 if __name__ == "__main__":

@@ -8,18 +8,22 @@
  * point is asynchronous on the given stream and performs no implicit device
  * synchronisation; functions that must read device state say so.
  *
- * Memory layout of a KV pool (fp16, page-major):
+ * Memory layout of a KV pool (fp16, layer-major):
  *
- *   page p, layer l, kv head h, K-or-V kv, slot s, element d lives at byte
- *     base + p*page_bytes + l*layer_bytes + h*head_bytes
+ *   layer l, page p, kv head h, K-or-V kv, slot s, element d lives at byte
+ *     base + l*layer_stride + p*seg_bytes + h*head_bytes
  *          + kv*(page_tokens*head_dim*2) + (s*head_dim + d)*2
- *   head_bytes  = 2 * page_tokens * head_dim * 2      (K block then V block)
- *   layer_bytes = num_kv_heads * head_bytes
- *   page_bytes  = num_layers * layer_bytes
+ *   head_bytes   = 2 * page_tokens * head_dim * 2     (K block then V block)
+ *   seg_bytes    = num_kv_heads * head_bytes          (one page, one layer)
+ *   layer_stride = num_pages * seg_bytes              (one layer, all pages)
+ *   page_bytes   = num_layers * seg_bytes             (one page, all layers)
  *
- * A physical page therefore holds `page_tokens` tokens of every layer, one
- * block-table entry addresses all layers, and a page is one contiguous byte
- * range (swap and copy move whole pages with single copies).
+ * One block-table entry addresses a page in every layer.  One layer's pages
+ * form one contiguous region, so a decode launch (one layer) touches a region
+ * of num_pages*seg_bytes rather than the whole pool.  Swap and copy move a page
+ * as num_layers strided segments; a host swap buffer holds page_bytes per page
+ * with the page's layer segments in layer order.  A raw byte pool
+ * (cfg.page_bytes != 0) is one contiguous page after another.
  *
  * Error convention: every function returns a vk_status (VK_OK = 0) and never
  * exits the process; vk_last_error_string() describes the last failure on the
@@ -99,10 +103,12 @@ vk_status vk_pool_check(vk_pool* pool, uint32_t* out_bits);
 vk_status vk_alloc_pages(vk_pool* pool, int32_t n, int32_t* out_ids);
 
 /* MemoryManager::free_block (cuda/memory.cu:137-143): ids outside the pool or
- * already free are ignored; any host swap copy recorded for the id is dropped. */
+ * already free are ignored.  (Host swap buffers belong to the caller, who drops
+ * the copy of a freed id, as the reference's free_block does.) */
 vk_status vk_free_pages(vk_pool* pool, const int32_t* ids, int32_t n);
 
-/* MemoryManager::get_block_ptr (cuda/memory.cu:145-150): NULL on a bad id. */
+/* MemoryManager::get_block_ptr (cuda/memory.cu:145-150): NULL on a bad id.
+ * Byte pools: base + id*page_bytes.  KV pools: the page's layer-0 segment. */
 void* vk_page_ptr(const vk_pool* pool, int32_t id);
 
 /* MemoryManager::blocks_in_use / blocks_available / total_allocated_bytes
@@ -157,6 +163,40 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
 int32_t   vk_decode_pages_per_split(const vk_pool* pool, int32_t batch, int32_t max_seq_len);
 vk_status vk_set_decode_split(vk_pool* pool, int32_t pages_per_split);
 
+/* ---- K2, planned: persistent load-balanced decode with fused append -------
+ * The same computation as vk_decode (and the append of vk_append for one new
+ * token per sequence), organised by a host-side plan.  A decode step's
+ * sequence lengths are known on the host and are the same for every layer, so
+ * the plan is built once per step:
+ *   vk_decode_plan_create(pool, seq_lens_host, B, Hq, &plan)   host only
+ *   vk_decode_plan_upload(plan, ws, ws_bytes, stream)          tables -> ws
+ *   for each layer: vk_decode_run(pool, plan, layer, ...)      one launch
+ * The plan cuts the pages of all (sequence, KV head) pairs into equal
+ * contiguous ranges, one per resident warp of the GPU.  seq_lens_host[b] is
+ * the number of tokens to attend, including the token being appended.
+ * k_new, v_new: [B, Hkv, D] fp16 rows of the token at position
+ * seq_lens_host[b]-1, written into the pool before it is read; pass NULL for
+ * both to attend without appending.  The page receiving the new token must not
+ * be shared with another sequence.  The workspace passed to vk_decode_run must
+ * hold the uploaded plan; runs on it must not overlap on the GPU. */
+typedef struct vk_decode_plan vk_decode_plan;
+
+vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_host, int32_t batch,
+                                int32_t num_q_heads, vk_decode_plan** out_plan);
+vk_status vk_decode_plan_destroy(vk_decode_plan* plan);
+size_t    vk_decode_plan_workspace_size(const vk_decode_plan* plan);
+/* Copies the plan's tables into the workspace (256-byte aligned) and zeroes its
+ * merge counters, asynchronously on `stream`. */
+vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace,
+                                size_t workspace_bytes, void* stream);
+/* Plan facts: 0 workers, 1 CTAs, 2 partial slots, 3 total pages, 4 longest
+ * sequence in pages; -1 for an unknown query. */
+int32_t   vk_decode_plan_info(const vk_decode_plan* plan, int32_t what);
+vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer, const void* q,
+                        void* out, const int32_t* block_tables, int32_t bt_stride,
+                        const void* k_new, const void* v_new, float scale, void* workspace,
+                        void* stream);
+
 /* ---- K3: chunked prefill -------------------------------------------------
  * The prefill use of launch_attention (src/transformer.cpp:136-189 with
  * num_tokens = chunk, src/engine.cpp:70-101): query token t of sequence b sits
@@ -189,8 +229,9 @@ vk_status vk_compact_plan(vk_pool* pool, int32_t* src_ids, int32_t* dst_ids, int
 
 /* ---- K5: pinned-host swap -------------------------------------------------
  * MemoryManager::swap_to_cpu (cuda/memory.cu:152-169): copies pages ids[0..n)
- * into host_buf (page i at host_buf + i*page_bytes; page-locked memory for an
- * asynchronous copy) on `stream`, then frees the ids.  The ids may be handed
+ * into host_buf (page i at host_buf + i*page_bytes, its layer segments in layer
+ * order; page-locked memory for an asynchronous copy) on `stream`, then frees
+ * the ids.  The ids may be handed
  * out again at once; work that writes them must be ordered after `stream`. */
 vk_status vk_swap_out(vk_pool* pool, const int32_t* ids, int32_t n, void* host_buf,
                       void* stream);

@@ -52,7 +52,7 @@ def lib():
         L.or_append_paged.argtypes = ([_u16p] + [_c_int] * 6 + [_u16p, _u16p, _i32p, _c_int, _i32p]
                                       + [_c_int, _c_int])
         L.or_append_paged.restype = _c_int
-        L.or_copy_pages.argtypes = [_u8p, ctypes.c_uint64, _c_int, _i32p, _i32p, _c_int]
+        L.or_copy_pages.argtypes = [_u8p, _c_int, ctypes.c_uint64, ctypes.c_uint64, _c_int, _i32p, _i32p, _c_int]
         L.or_copy_pages.restype = _c_int
         L.or_remap_block_tables.argtypes = [_i32p, ctypes.c_int64, _i32p, _c_int]
         L.or_remap_block_tables.restype = None
@@ -88,8 +88,14 @@ class Geom:
     def page_elems(self):
         return self.L * self.Hkv * 2 * self.P * self.D
 
+    @property
+    def seg_bytes(self):
+        """Bytes of one page in one layer."""
+        return self.Hkv * 2 * self.P * self.D * 2
+
     def pool_shape(self):
-        return (self.num_pages, self.L, self.Hkv, 2, self.P, self.D)
+        """Layer-major pool: [layer, page, kv head, K|V, slot, d]."""
+        return (self.L, self.num_pages, self.Hkv, 2, self.P, self.D)
 
 
 def attention_causal(Q, K, V):
@@ -152,9 +158,10 @@ def append_paged(pool_u16, g: Geom, layer, k_u16, v_u16, block_tables, positions
                                  block_tables.shape[1], np.ascontiguousarray(positions, np.int32), B, T)
 
 
-def copy_pages(pool_bytes, page_bytes, num_pages, src, dst):
+def copy_pages(pool_bytes, nseg, seg_bytes, seg_stride, num_pages, src, dst):
+    """In-place page copy on a host byte image of the pool (see or_copy_pages)."""
     flat = pool_bytes.reshape(-1)
-    rc = lib().or_copy_pages(flat, page_bytes, num_pages, np.ascontiguousarray(src, np.int32),
+    rc = lib().or_copy_pages(flat, nseg, seg_bytes, seg_stride, num_pages, np.ascontiguousarray(src, np.int32),
                              np.ascontiguousarray(dst, np.int32), len(src))
     if rc != 0:
         raise ValueError("oracle copy: bad id")

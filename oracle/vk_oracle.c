@@ -103,8 +103,8 @@ typedef struct {
 
 static inline int64_t or_row_off(const or_geom* g, int64_t page, int layer, int head, int kv,
                                  int slot) {
-    /* element offset of row (page, layer, head, kv, slot) */
-    int64_t chunk = ((page * g->L + layer) * (int64_t)g->Hkv + head);
+    /* element offset of row (layer, page, head, kv, slot): layer-major pool */
+    int64_t chunk = (((int64_t)layer * g->num_pages + page) * g->Hkv + head);
     return ((chunk * 2 + kv) * g->P + slot) * (int64_t)g->D;
 }
 
@@ -278,15 +278,19 @@ int or_append_paged(uint16_t* pool, int L, int Hkv, int D, int P, int num_pages,
     return bad ? -1 : 0;
 }
 
-/* Page copy: dst_ids[i] <- src_ids[i], whole pages, applied in order. */
-int or_copy_pages(uint8_t* pool, uint64_t page_bytes, int num_pages, const int32_t* src_ids,
-                  const int32_t* dst_ids, int n) {
+/* Page copy: dst_ids[i] <- src_ids[i], whole pages, applied in order.  A page
+ * is nseg segments of seg_bytes; segment s of page id is at
+ * s*seg_stride + id*seg_bytes (one segment per layer of a KV pool; a byte pool
+ * has one segment). */
+int or_copy_pages(uint8_t* pool, int nseg, uint64_t seg_bytes, uint64_t seg_stride, int num_pages,
+                  const int32_t* src_ids, const int32_t* dst_ids, int n) {
     for (int i = 0; i < n; ++i) {
         if (src_ids[i] < 0 || src_ids[i] >= num_pages || dst_ids[i] < 0 ||
             dst_ids[i] >= num_pages)
             return -1;
-        memmove(pool + (uint64_t)dst_ids[i] * page_bytes, pool + (uint64_t)src_ids[i] * page_bytes,
-                (size_t)page_bytes);
+        for (int s = 0; s < nseg; ++s)
+            memmove(pool + (uint64_t)s * seg_stride + (uint64_t)dst_ids[i] * seg_bytes,
+                    pool + (uint64_t)s * seg_stride + (uint64_t)src_ids[i] * seg_bytes, (size_t)seg_bytes);
     }
     return 0;
 }

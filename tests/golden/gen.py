@@ -1,7 +1,8 @@
 """Seeded synthetic inputs shared by the fixture generator and the tests.
 
 Values are fp16 draws of N(0, 0.5^2) from numpy's PCG64 generator; block
-tables are seeded permutations of the physical page ids.  Only the slots that a
+tables are seeded permutations of the physical page ids.  Pools are layer-major
+[layer, page, kv head, K|V, slot, d], the library's device layout.  Only the slots that a
 case uses are filled (the rest stay zero), as a freshly created pool is
 zero-filled.
 """
@@ -34,7 +35,7 @@ def fill_sequences(rng, pool, g, layer, bt, lens):
     for b, n in enumerate(lens):
         for j in range(int(n)):
             page = bt[b][j // g.P]
-            pool[page, layer, :, :, j % g.P, :] = normal_f16(rng, (g.Hkv, 2, g.D))
+            pool[layer, page, :, :, j % g.P, :] = normal_f16(rng, (g.Hkv, 2, g.D))
 
 
 def paged_case(index):

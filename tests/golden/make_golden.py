@@ -54,8 +54,8 @@ def ref_decode_rows(pool, g, layer, q, bt, lens):
         pages = bt[b][idx // g.P]
         for h in range(Hq):
             kv = h // G
-            K = pool[pages, layer, kv, 0, idx % g.P].astype(np.float32)
-            V = pool[pages, layer, kv, 1, idx % g.P].astype(np.float32)
+            K = pool[layer, pages, kv, 0, idx % g.P].astype(np.float32)
+            V = pool[layer, pages, kv, 1, idx % g.P].astype(np.float32)
             Q = np.zeros((n, D), np.float32)
             Q[n - 1] = q[b, h].astype(np.float32)
             out[b, h] = oracle.ref_attention_causal(Q[None, None], K[None, None], V[None, None])[0, 0, n - 1]

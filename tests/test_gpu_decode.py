@@ -66,8 +66,8 @@ def test_append_f32_rounds_to_nearest_even(vk):
     ref = x.astype(np.float16)
     for t in range(20):
         page, slot = bt[0][t // 16], t % 16
-        assert np.array_equal(kv[page, 0, :, 0, slot].view(np.uint16), ref[0, t].view(np.uint16))
-        assert np.array_equal(kv[page, 0, :, 1, slot].view(np.uint16), (-x[0, t]).astype(np.float16).view(np.uint16))
+        assert np.array_equal(kv[0, page, :, 0, slot].view(np.uint16), ref[0, t].view(np.uint16))
+        assert np.array_equal(kv[0, page, :, 1, slot].view(np.uint16), (-x[0, t]).astype(np.float16).view(np.uint16))
 
 
 def test_append_rejects_bad_entries(vk):
@@ -141,7 +141,7 @@ def test_decode_ignores_poisoned_slots(vk):
     host = random_pool(rng, g, fill_nan=True)
     for b, n in enumerate(lens):
         for j in range(n):
-            host[bt[b][j // 16], 0, :, :, j % 16, :] = (rng.standard_normal((2, 2, 128)) * 0.5).astype(np.float16)
+            host[0, bt[b][j // 16], :, :, j % 16, :] = (rng.standard_normal((2, 2, 128)) * 0.5).astype(np.float16)
     pool = make_pool(vk, g, host)
     q = (rng.standard_normal((4, 8, 128)) * 0.5).astype(np.float16)
     ref = oracle.decode_paged(host.view(np.uint16), g, 0, q.view(np.uint16), bt, lens)
@@ -158,7 +158,7 @@ def test_decode_single_key_returns_v0(vk):
     pool = make_pool(vk, g, host)
     q = (rng.standard_normal((1, 8, 128)) * 3).astype(np.float16)
     out = run_decode(vk, pool, 0, q, np.array([[2]], np.int32), np.array([1], np.int32))
-    v0 = host[2, 0, :, 1, 0].astype(np.float32)  # [Hkv, D]
+    v0 = host[0, 2, :, 1, 0].astype(np.float32)  # [Hkv, D]
     assert np.array_equal(out[0], np.repeat(v0, 4, axis=0))
 
 
@@ -173,7 +173,7 @@ def test_decode_convex_bound(vk):
     q = (rng.standard_normal((2, 8, 128))).astype(np.float16)
     out = run_decode(vk, pool, 0, q, bt, lens, pps=1)
     for b, n in enumerate(lens):
-        vs = np.stack([host[bt[b][j // 16], 0, 0, 1, j % 16] for j in range(n)]).astype(np.float32)
+        vs = np.stack([host[0, bt[b][j // 16], 0, 1, j % 16] for j in range(n)]).astype(np.float32)
         assert out[b].min() >= vs.min() - 1e-3 and out[b].max() <= vs.max() + 1e-3
 
 
@@ -201,7 +201,7 @@ def test_decode_page_permutation_invariance(vk):
     host = random_pool(rng, g)
     perm = rng.permutation(g.num_pages)
     host2 = np.empty_like(host)
-    host2[perm] = host
+    host2[:, perm] = host
     bt2 = np.where(bt >= 0, perm[np.maximum(bt, 0)], -1).astype(np.int32)
     q = (rng.standard_normal((2, 8, 128)) * 0.5).astype(np.float16)
     p1, p2 = make_pool(vk, g, host), make_pool(vk, g, host2)

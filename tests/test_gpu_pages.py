@@ -29,7 +29,7 @@ def test_copy_pages_bit_exact(vk):
     pool.copy_pages(dev_i32(src), dev_i32(dst))
     assert pool.check() == 0
     expect = host.copy()
-    oracle.copy_pages(expect.view(np.uint8).reshape(g.num_pages, -1), pool.page_bytes, g.num_pages, src, dst)
+    oracle.copy_pages(expect.view(np.uint8), g.L, g.seg_bytes, g.seg_bytes * g.num_pages, g.num_pages, src, dst)
     assert np.array_equal(pool.kv_view().cpu().numpy().view(np.uint16), expect.view(np.uint16))
 
 
@@ -88,10 +88,11 @@ def test_swap_round_trip_and_remap(vk):
     s.synchronize()
     assert pool.pages_in_use() == 12
     assert [pool.page_in_use(i) for i in victims] == [0, 0, 0, 0]
-    expect = host.view(np.uint8).reshape(16, -1)[victims].reshape(-1)
+    # host buffer: whole pages back to back, each page's layer segments in order
+    expect = np.ascontiguousarray(host.transpose(1, 0, 2, 3, 4, 5)[victims]).view(np.uint8).reshape(-1)
     assert np.array_equal(pinned.numpy(), expect)
     # scribble over the freed pages, then swap back in (lowest free ids first)
-    pool.kv_view()[victims] = 0
+    pool.kv_view()[:, victims] = 0
     got_ids = pool.swap_in(pinned, 4)
     torch.cuda.synchronize()
     assert got_ids == victims
@@ -170,7 +171,7 @@ def test_kvcache_mirror(vk):
     kp, vp = c.get(0)
     assert kp and vp and vp - kp == 16 * head_dim * 2
     page = c.block_table[0, 0].item()
-    kv = c.pool.kv_view()[page, 0]
+    kv = c.pool.kv_view()[0, page]
     assert torch.equal(kv[:, 0, 0].float().cpu().reshape(-1), k.cpu().reshape(-1))
     assert torch.equal(kv[:, 1, 0].float().cpu().reshape(-1), v.cpu().reshape(-1))
     c.append(5, k, v, 0, 1)                                            # bad layer: ignored

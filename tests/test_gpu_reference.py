@@ -126,7 +126,7 @@ def test_kvcache_append_matches_reference(ref, vk):
         ref.ref_kv_get(rc, 1, ctypes.byref(kp), ctypes.byref(vpp))
         rk = device_view(kp.value, Hkv * S * D * 4).view(torch.float32).view(Hkv, S, D).cpu()
         rv = device_view(vpp.value, Hkv * S * D * 4).view(torch.float32).view(Hkv, S, D).cpu()
-        kv = c.pool.kv_view()[:, 1].cpu()  # [pages, Hkv, 2, 16, D]
+        kv = c.pool.kv_view()[1].cpu()  # [pages, Hkv, 2, 16, D]
         bt = c.block_table[0].cpu()
         for j in range(pos):
             page = int(bt[j // 16])

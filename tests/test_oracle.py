@@ -123,9 +123,9 @@ def test_oracle_append_scatter_rule():
         for t in range(T):
             p = pos[b] + t
             for h in range(2):
-                assert np.array_equal(pool[bt[b][p // 16], 2, h, 0, p % 16], k[b, t, h])
-                assert np.array_equal(pool[bt[b][p // 16], 2, h, 1, p % 16], v[b, t, h])
-    assert np.count_nonzero(pool[:, :2]) == 0  # other layers untouched
+                assert np.array_equal(pool[2, bt[b][p // 16], h, 0, p % 16], k[b, t, h])
+                assert np.array_equal(pool[2, bt[b][p // 16], h, 1, p % 16], v[b, t, h])
+    assert np.count_nonzero(pool[:2]) == 0  # other layers untouched
     # overflow past the table: reported, nothing written for that token
     pool2 = np.zeros_like(pool)
     assert oracle.append_paged(pool2, g, 0, k, v, bt, np.array([44, 0], np.int32)) == -1
@@ -135,9 +135,14 @@ def test_oracle_copy_and_remap():
     page = 64
     pool = np.arange(10 * page, dtype=np.uint32).astype(np.uint8).reshape(10, page)
     before = pool.copy()
-    oracle.copy_pages(pool, page, 10, np.array([7, 8], np.int32), np.array([1, 2], np.int32))
+    oracle.copy_pages(pool, 1, page, 0, 10, np.array([7, 8], np.int32), np.array([1, 2], np.int32))
     assert np.array_equal(pool[1], before[7]) and np.array_equal(pool[2], before[8])
     assert np.array_equal(pool[7], before[7])
+    # three layer segments of 16 bytes per page (layer-major)
+    seg = np.arange(3 * 10 * 16, dtype=np.uint32).astype(np.uint8).reshape(3, 10, 16)
+    before = seg.copy()
+    oracle.copy_pages(seg, 3, 16, 160, 10, np.array([9], np.int32), np.array([0], np.int32))
+    assert np.array_equal(seg[:, 0], before[:, 9]) and np.array_equal(seg[:, 1:], before[:, 1:])
     bt = np.array([[7, 3, -1], [8, 9, 0]], np.int32)
     pm = np.arange(10, dtype=np.int32)
     pm[7], pm[8] = 1, 2

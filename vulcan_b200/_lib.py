@@ -53,6 +53,12 @@ SIGNATURES = {
                           vp]),
     "vk_decode_static": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
     "vk_decode_pages_per_split": (c_i32, [vp, c_i32, c_i32]),
+    "vk_decode_plan_create": (c_i32, [vp, i32p, c_i32, c_i32, ctypes.POINTER(vp)]),
+    "vk_decode_plan_destroy": (c_i32, [vp]),
+    "vk_decode_plan_workspace_size": (c_sz, [vp]),
+    "vk_decode_plan_upload": (c_i32, [vp, vp, c_sz, vp]),
+    "vk_decode_plan_info": (c_i32, [vp, c_i32]),
+    "vk_decode_run": (c_i32, [vp, vp, c_i32, vp, vp, vp, c_i32, vp, vp, c_f32, vp, vp]),
     "vk_set_decode_split": (c_i32, [vp, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
     "vk_copy_pages": (c_i32, [vp, vp, vp, c_i32, vp]),

@@ -19,7 +19,7 @@ struct AppendParams {
     const int32_t* bt;
     const int32_t* pos;
     uint32_t* err;
-    uint64_t page_bytes, layer_off, head_bytes;
+    uint64_t seg_bytes, layer_off, head_bytes;
     int bt_stride, B, T, Hkv, D, P, num_pages;
 };
 
@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
         if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
         return;
     }
-    char* dst_k = p.base + static_cast<uint64_t>(page) * p.page_bytes + p.layer_off +
+    char* dst_k = p.base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
                   static_cast<uint64_t>(h) * p.head_bytes +
                   static_cast<uint64_t>(pos % p.P) * p.D * 2;
     char* dst_v = dst_k + static_cast<uint64_t>(p.P) * p.D * 2;
@@ -85,8 +85,8 @@ vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, 
     p.bt = bt;
     p.pos = pos;
     p.err = pool->d_err;
-    p.page_bytes = pool->page_bytes;
-    p.layer_off = static_cast<uint64_t>(layer) * pool->layer_bytes;
+    p.seg_bytes = pool->seg_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
     p.head_bytes = pool->head_bytes;
     p.bt_stride = bt_stride;
     p.B = B;
@@ -112,22 +112,25 @@ constexpr int kCopyThreads = 512;
 constexpr int kCopyUnroll = 4;
 constexpr uint64_t kCopyChunk = static_cast<uint64_t>(kCopyThreads) * kCopyUnroll * 16;  // 32 KiB
 
-// grid.x = chunks per page, grid.y = page pairs.  Each CTA moves one 32 KiB
-// chunk of one page with 16-byte loads issued ahead of the stores.
-__global__ void __launch_bounds__(kCopyThreads) copy_pages_kernel(char* base, uint64_t page_bytes,
-                                                                  const int32_t* src,
-                                                                  const int32_t* dst, int num_pages,
-                                                                  uint32_t* err) {
+// grid.x = (32 KiB chunks of a segment) x segments, grid.y = page pairs.  Each
+// CTA moves one chunk of one layer segment of one page with 16-byte loads
+// issued ahead of the stores.
+__global__ void __launch_bounds__(kCopyThreads) copy_pages_kernel(char* base, uint64_t seg_bytes,
+                                                                  uint64_t seg_stride, int chunks_per_seg,
+                                                                  const int32_t* src, const int32_t* dst,
+                                                                  int num_pages, uint32_t* err) {
     const int pair = blockIdx.y;
     const int32_t s = src[pair], d = dst[pair];
     if (s < 0 || s >= num_pages || d < 0 || d >= num_pages) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, VK_ERR_PAGE_ID);
         return;
     }
-    const uint64_t off = static_cast<uint64_t>(blockIdx.x) * kCopyChunk;
-    const uint4* sp = reinterpret_cast<const uint4*>(base + static_cast<uint64_t>(s) * page_bytes + off);
-    uint4* dp = reinterpret_cast<uint4*>(base + static_cast<uint64_t>(d) * page_bytes + off);
-    const uint64_t left = page_bytes - off;
+    const int seg = blockIdx.x / chunks_per_seg;
+    const uint64_t off = static_cast<uint64_t>(blockIdx.x % chunks_per_seg) * kCopyChunk;
+    const uint64_t seg_off = static_cast<uint64_t>(seg) * seg_stride;
+    const uint4* sp = reinterpret_cast<const uint4*>(base + seg_off + static_cast<uint64_t>(s) * seg_bytes + off);
+    uint4* dp = reinterpret_cast<uint4*>(base + seg_off + static_cast<uint64_t>(d) * seg_bytes + off);
+    const uint64_t left = seg_bytes - off;
     const int nvec = static_cast<int>((left < kCopyChunk ? left : kCopyChunk) / 16);
     uint4 r[kCopyUnroll];
 #pragma unroll
@@ -144,13 +147,15 @@ __global__ void __launch_bounds__(kCopyThreads) copy_pages_kernel(char* base, ui
 
 vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* dst, int n,
                             cudaStream_t st) {
-    if (pool->page_bytes % 16) return fail(VK_UNSUPPORTED, "copy needs page_bytes % 16 == 0");
+    if (pool->seg_bytes % 16) return fail(VK_UNSUPPORTED, "copy needs page segments of a multiple of 16 bytes");
     if (n > 65535) return fail(VK_INVALID_ARG, "copy_pages: at most 65535 pages per call");
-    const uint64_t chunks = (pool->page_bytes + kCopyChunk - 1) / kCopyChunk;
-    if (chunks > 0x7fffffff) return fail(VK_INVALID_ARG, "page too large");
-    dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(n));
-    copy_pages_kernel<<<grid, kCopyThreads, 0, st>>>(pool->base, pool->page_bytes, src, dst,
-                                                     pool->num_pages, pool->d_err);
+    const uint64_t chunks = (pool->seg_bytes + kCopyChunk - 1) / kCopyChunk;
+    const uint64_t blocks = chunks * static_cast<uint64_t>(pool->nseg);
+    if (blocks > 0x7fffffff) return fail(VK_INVALID_ARG, "page too large");
+    dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(n));
+    copy_pages_kernel<<<grid, kCopyThreads, 0, st>>>(pool->base, pool->seg_bytes, pool->seg_stride,
+                                                     static_cast<int>(chunks), src, dst, pool->num_pages,
+                                                     pool->d_err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "copy_pages_kernel launch");
 }

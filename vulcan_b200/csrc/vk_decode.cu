@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
                     atomicOr(p.err, VK_ERR_PAGE_ID);
                     page = 0;
                 }
-                const int row = ((page * p.L + p.layer) * p.Hkv + hkv) * (2 * P);
+                const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
                 const uint32_t bar = smem_u32(&full[st]);
                 mbar_expect_tx(bar, SB);
                 const uint32_t dst = smem_u32(smem + st * SB);

@@ -1,0 +1,574 @@
+// Planned paged GQA decode: a persistent kernel over a host-built balanced
+// schedule, with the new token's K/V append and the split merge fused in.
+//
+// Same arithmetic and result as vk_decode (one causal row of the reference's
+// cpu_attention per query head, tests/test_attention.cu:66-97, over the paged
+// cache; GQA mapping of src/transformer.cpp:173-179), organised for the B200:
+//
+//  * The plan (host, once per decode step since every layer of a step has the
+//    same lengths) lays the pages of all (sequence, KV head) units end to end
+//    and cuts that list into W equal contiguous ranges, one per warp ("worker"),
+//    with W = resident warps of the GPU.  Every worker streams the same number
+//    of pages, so there is no tail of long sequences and no per-split CTA
+//    prologue; ranges cross unit boundaries freely.
+//  * Each worker warp prefetches its own pages NSTW ahead with 2-D TMA loads
+//    (one mbarrier per stage) and folds each page into its softmax state with
+//    the tensor-core page update shared with vk_decode.
+//  * Append fused: when a worker is about to load the last page of a unit and
+//    new K/V rows were given, the warp first writes the new token's rows into
+//    that page (fence.proxy.async orders them before the TMA read).
+//  * Merge fused: a unit covered by one worker writes its fp16 output directly;
+//    otherwise each piece writes its normalised partial and log2-sum-exp, and
+//    the last piece to finish (per-unit counter) merges them from L2 and resets
+//    the counter for the next launch.
+#include <algorithm>
+#include <vector>
+
+#include "vk_decode_page.cuh"
+#include "vk_internal.h"
+
+namespace vk {
+
+constexpr int kPlanWarps = 2;      // worker warps per CTA
+constexpr int kPlanStages = 4;     // TMA stages per worker (8 KiB each at D=128)
+constexpr int kMinPagesPerWorker = 8;
+
+struct PlanParams {
+    const int32_t* wb;     // [W+1] first global page of each worker
+    const int32_t* wfu;    // [W]   unit holding the worker's first page
+    const int32_t* uoff;   // [U+1] first global page of each unit
+    const int32_t* ulen;   // [U]   tokens of the unit's sequence
+    const int32_t* ufw;    // [U]   first worker touching the unit
+    const int32_t* unp;    // [U]   workers touching the unit (pieces)
+    const int32_t* uslot;  // [U]   first partial slot of the unit (-1 if one piece)
+    const int32_t* zunits; // [Z]   units without pages (zero output)
+    uint32_t* counters;    // [U]   pieces finished (reset by the merging piece)
+    float* part_o;         // [slots, G, D]
+    float* part_lse;       // [slots, G]
+    const __half* q;
+    __half* out;
+    const __half* k_new;   // [B, Hkv, D] or null
+    const __half* v_new;
+    const int32_t* bt;
+    uint32_t* err;
+    char* pool_base;
+    uint64_t seg_bytes, layer_off, head_bytes;
+    int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z;
+    float scale_log2;
+};
+
+template <int D>
+__host__ __device__ constexpr int plan_smem_bytes() {
+    return kPlanWarps * kPlanStages * (2 * kPageTokens * D * 2) + kPlanWarps * kPlanStages * 8 + 1024;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Iterator over (unit, page-in-unit) along the concatenated page list.
+struct PageIt {
+    int u, p, np;
+    __device__ __forceinline__ void next(const int32_t* uoff) {
+        if (++p == np) {
+            p = 0;
+            do {
+                ++u;
+                np = uoff[u + 1] - uoff[u];
+            } while (np == 0);
+        }
+    }
+};
+
+// The last piece of a unit combines all pieces' partials (read from L2):
+// out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), streamed over k with a
+// running max.  Each lane owns float4 items f = lane + 32*i of the unit's
+// [G, D] output; all loads of one piece are issued together, so the merge costs
+// about one L2 round trip per piece.
+template <int D, int NT>
+__device__ __forceinline__ void merge_pieces(const PlanParams& p, int base, int npieces, int64_t head0, int lane) {
+    constexpr int ITEMS = NT * 8 * D / 128;  // float4 items per lane for G = 8*NT
+    constexpr int ROUND = ITEMS < 8 ? ITEMS : 8;
+    const int nf = p.G * D / 4;
+    const float* lse = p.part_lse + static_cast<int64_t>(base) * p.G;
+    const float4* os = reinterpret_cast<const float4*>(p.part_o + static_cast<int64_t>(base) * p.G * D);
+    for (int i0 = 0; i0 < ITEMS; i0 += ROUND) {
+        float m[ROUND], den[ROUND];
+        float4 acc[ROUND];
+        int h[ROUND];
+#pragma unroll
+        for (int i = 0; i < ROUND; ++i) {
+            m[i] = -INFINITY;
+            den[i] = 0.f;
+            acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int f = lane + 32 * (i0 + i);
+            h[i] = f < nf ? (f * 4) / D : 0;
+        }
+        for (int k = 0; k < npieces; ++k) {
+            float l[ROUND];
+            float4 o[ROUND];
+#pragma unroll
+            for (int i = 0; i < ROUND; ++i) {
+                const int f = lane + 32 * (i0 + i);
+                const int fc = f < nf ? f : 0;
+                l[i] = __ldcg(lse + k * p.G + h[i]);
+                o[i] = __ldcg(os + static_cast<int64_t>(k) * nf + fc);
+            }
+#pragma unroll
+            for (int i = 0; i < ROUND; ++i) {
+                const float mn = fmaxf(m[i], l[i]);
+                const float a = ex2(m[i] - mn), b = ex2(l[i] - mn);
+                den[i] = den[i] * a + b;
+                acc[i].x = acc[i].x * a + b * o[i].x;
+                acc[i].y = acc[i].y * a + b * o[i].y;
+                acc[i].z = acc[i].z * a + b * o[i].z;
+                acc[i].w = acc[i].w * a + b * o[i].w;
+                m[i] = mn;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < ROUND; ++i) {
+            const int f = lane + 32 * (i0 + i);
+            if (f < nf) {
+                const float inv = 1.f / den[i];
+                __half2* dst = reinterpret_cast<__half2*>(p.out + head0 * D + f * 4);
+                dst[0] = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
+                dst[1] = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
+            }
+        }
+    }
+}
+
+template <int D, int NT>
+__global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                         const PlanParams p) {
+    constexpr int P = kPageTokens;
+    constexpr int SB = 2 * P * D * 2;
+    constexpr int NB = D / 64;
+    constexpr int KS = D / 16;
+    constexpr int NS = kPlanStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPlanWarps * NS * SB);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = blockIdx.x * kPlanWarps + warp;
+
+    // Units without pages: zero output (spread over all warps of the grid).
+    for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
+        const int u = p.zunits[i];
+        __half* o = p.out + (static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G) * D;
+        for (int e = lane; e < p.G * D; e += 32) o[e] = __float2half(0.f);
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPlanWarps * NS; ++s) mbar_init(smem_u32(&bars[s]), 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (w >= p.W) return;
+    const int g0 = p.wb[w];
+    const int n = p.wb[w + 1] - g0;
+    if (n <= 0) return;
+
+    uint8_t* my_stages = smem + warp * NS * SB;
+    uint64_t* full = bars + warp * NS;
+    if (lane == 0) prefetch_tmap(&tmap);
+    const uint64_t pol = l2_evict_first_policy();
+
+    const int u0 = p.wfu[w];
+    PageIt pf{u0, g0 - p.uoff[u0], p.uoff[u0 + 1] - p.uoff[u0]};  // prefetch cursor
+    PageIt cu = pf;                                                // consume cursor
+
+    // Loads page `pf` into stage s (whole warp; lane 0 issues the TMA).
+    auto issue = [&](int s) {
+        const int b = pf.u / p.Hkv, hkv = pf.u % p.Hkv;
+        int page = p.bt[static_cast<int64_t>(b) * p.bt_stride + pf.p];
+        if (page < 0 || page >= p.num_pages) {
+            if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
+            page = 0;
+        } else if (p.k_new != nullptr && pf.p == pf.np - 1) {
+            // fused append of the token at position len-1 into this page
+            const int slot = (p.ulen[pf.u] - 1) % P;
+            char* dk = p.pool_base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
+                       static_cast<uint64_t>(hkv) * p.head_bytes + static_cast<uint64_t>(slot) * D * 2;
+            const int64_t src = (static_cast<int64_t>(b) * p.Hkv + hkv) * D;
+            for (int v = lane; v < 2 * (D / 8); v += 32) {
+                const bool is_v = v >= D / 8;
+                const int vi = is_v ? v - D / 8 : v;
+                const uint4 val = __ldg(reinterpret_cast<const uint4*>((is_v ? p.v_new : p.k_new) + src) + vi);
+                reinterpret_cast<uint4*>(dk + (is_v ? P * D * 2 : 0))[vi] = val;
+            }
+            fence_proxy_async_global();
+            __syncwarp();
+        }
+        if (lane == 0) {
+            const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
+            const uint32_t bar = smem_u32(&full[s]);
+            mbar_expect_tx(bar, SB);
+            const uint32_t dst = smem_u32(my_stages + s * SB);
+#pragma unroll
+            for (int hb = 0; hb < NB; ++hb) tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+        }
+        pf.next(p.uoff);
+    };
+
+    const int pre = min(n, NS);
+    for (int j = 0; j < pre; ++j) issue(j);
+
+    uint32_t qf[NT][KS][2];
+    WarpSoftmaxState<D, NT> st;
+    load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D, p.G, lane);
+    st.reset();
+
+    for (int j = 0; j < n; ++j) {
+        const int s = j % NS;
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), (j / NS) & 1, p.err))) return;
+        const int valid = min(P, p.ulen[cu.u] - cu.p * P);
+        page_update<D, NT>(smem_u32(my_stages + s * SB), valid, qf, st, p.scale_log2, lane);
+        // Every lane's ldmatrix results for stage s have been consumed by its MMAs
+        // before __syncwarp returns, so the stage can be refilled.
+        __syncwarp();
+        if (j + NS < n) issue(s);
+
+        const bool unit_done = (cu.p == cu.np - 1) || (j == n - 1);
+        if (unit_done) {
+            // ------------------------------------------------ finish this piece of unit cu.u
+            reduce_l<D, NT>(st);
+            const int u = cu.u;
+            const int64_t head0 = static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G;
+            const int npieces = p.unp[u];
+            if (npieces == 1) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int h0 = nt * 8 + (lane & 3) * 2;
+                    const float i0 = 1.f / st.l[nt][0], i1 = 1.f / st.l[nt][1];
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        const int d = mt * 16 + (lane >> 2);
+                        if (h0 < p.G) {
+                            p.out[(head0 + h0) * D + d] = __float2half(st.acc[nt][mt][0] * i0);
+                            p.out[(head0 + h0) * D + d + 8] = __float2half(st.acc[nt][mt][2] * i0);
+                        }
+                        if (h0 + 1 < p.G) {
+                            p.out[(head0 + h0 + 1) * D + d] = __float2half(st.acc[nt][mt][1] * i1);
+                            p.out[(head0 + h0 + 1) * D + d + 8] = __float2half(st.acc[nt][mt][3] * i1);
+                        }
+                    }
+                }
+            } else {
+                const int base = p.uslot[u];
+                const int slot = base + (w - p.ufw[u]);
+                float* po = p.part_o + static_cast<int64_t>(slot) * p.G * D;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int h0 = nt * 8 + (lane & 3) * 2;
+                    const float i0 = 1.f / st.l[nt][0], i1 = 1.f / st.l[nt][1];
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        const int d = mt * 16 + (lane >> 2);
+                        if (h0 < p.G) {
+                            po[h0 * D + d] = st.acc[nt][mt][0] * i0;
+                            po[h0 * D + d + 8] = st.acc[nt][mt][2] * i0;
+                        }
+                        if (h0 + 1 < p.G) {
+                            po[(h0 + 1) * D + d] = st.acc[nt][mt][1] * i1;
+                            po[(h0 + 1) * D + d + 8] = st.acc[nt][mt][3] * i1;
+                        }
+                    }
+                    if (lane < 4) {
+                        if (h0 < p.G) p.part_lse[static_cast<int64_t>(slot) * p.G + h0] = st.m[nt][0] + __log2f(st.l[nt][0]);
+                        if (h0 + 1 < p.G) p.part_lse[static_cast<int64_t>(slot) * p.G + h0 + 1] = st.m[nt][1] + __log2f(st.l[nt][1]);
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                unsigned int prev = 0;
+                if (lane == 0) prev = atomicAdd(&p.counters[u], 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == static_cast<unsigned int>(npieces - 1)) {
+                    __threadfence();
+                    merge_pieces<D, NT>(p, base, npieces, head0, lane);
+                    if (lane == 0) atomicExch(&p.counters[u], 0u);
+                }
+            }
+            if (j + 1 < n) {
+                cu.next(p.uoff);
+                load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D,
+                                    p.G, lane);
+                st.reset();
+            }
+        } else {
+            cu.next(p.uoff);
+        }
+    }
+}
+
+template <int D, int NT>
+static int plan_occupancy(int device, int* occ_out) {
+    static int cache[64] = {};
+    if (device < 0 || device >= 64) return -1;
+    if (cache[device] == 0) {
+        constexpr int smem = plan_smem_bytes<D>();
+        if (cudaFuncSetAttribute(planned_decode_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return -1;
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, planned_decode_kernel<D, NT>, kPlanWarps * 32, smem) !=
+                cudaSuccess ||
+            occ <= 0)
+            return -1;
+        cache[device] = occ;
+    }
+    *occ_out = cache[device];
+    return 0;
+}
+
+static int occupancy_for(int D, int NT, int device, int* occ) {
+    if (D == 128) return NT == 1 ? plan_occupancy<128, 1>(device, occ) : plan_occupancy<128, 2>(device, occ);
+    if (D == 64) return NT == 1 ? plan_occupancy<64, 1>(device, occ) : plan_occupancy<64, 2>(device, occ);
+    return NT == 1 ? plan_occupancy<256, 1>(device, occ) : plan_occupancy<256, 2>(device, occ);
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace vk
+
+struct vk_decode_plan {
+    int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1;
+    int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
+    std::vector<int32_t> tables;
+    size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_z = 0;
+    size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
+};
+
+using namespace vk;
+
+extern "C" {
+
+vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_host, int32_t batch,
+                                int32_t num_q_heads, vk_decode_plan** out_plan) {
+    if (!out_plan) return fail(VK_INVALID_ARG, "out_plan is NULL");
+    *out_plan = nullptr;
+    if (!pool || !pool->kv) return fail(VK_INVALID_ARG, "plan needs a KV pool");
+    if (pool->cfg.page_tokens != kPageTokens) return fail(VK_UNSUPPORTED, "plan supports page_tokens == 16");
+    const int D = pool->cfg.head_dim, Hkv = pool->cfg.num_kv_heads;
+    if (D != 64 && D != 128 && D != 256) return fail(VK_UNSUPPORTED, "plan supports head_dim 64, 128, 256");
+    if (batch < 0 || (batch > 0 && !seq_lens_host)) return fail(VK_INVALID_ARG, "bad batch / seq_lens");
+    if (num_q_heads <= 0 || num_q_heads % Hkv) return fail(VK_INVALID_ARG, "num_q_heads must be a positive multiple of num_kv_heads");
+    const int G = num_q_heads / Hkv;
+    if (G > 16) return fail(VK_UNSUPPORTED, "plan supports up to 16 query heads per KV head");
+    auto* pl = new vk_decode_plan();
+    pl->device = pool->device;
+    pl->B = batch;
+    pl->Hq = num_q_heads;
+    pl->Hkv = Hkv;
+    pl->G = G;
+    pl->D = D;
+    pl->NT = G <= 8 ? 1 : 2;
+    const int U = batch * Hkv;
+    pl->U = U;
+    std::vector<int64_t> uoff(static_cast<size_t>(U) + 1, 0);
+    std::vector<int32_t> ulen(U), zunits;
+    for (int b = 0; b < batch; ++b) {
+        if (seq_lens_host[b] < 0) {
+            delete pl;
+            return fail(VK_INVALID_ARG, "negative sequence length");
+        }
+        const int np = (seq_lens_host[b] + kPageTokens - 1) / kPageTokens;
+        pl->max_unit_pages = std::max(pl->max_unit_pages, np);
+        for (int h = 0; h < Hkv; ++h) {
+            const int u = b * Hkv + h;
+            ulen[u] = seq_lens_host[b];
+            uoff[u + 1] = uoff[u] + np;
+            if (np == 0) zunits.push_back(u);
+        }
+    }
+    const int64_t T = uoff[U];
+    if (T >= (1ll << 31)) {
+        delete pl;
+        return fail(VK_INVALID_ARG, "too many pages in one step");
+    }
+    pl->total_pages = static_cast<int>(T);
+    pl->Z = static_cast<int>(zunits.size());
+    int occ = 1;
+    {
+        DeviceGuard g(pool->device);
+        if (occupancy_for(D, pl->NT, pool->device, &occ) != 0) {
+            delete pl;
+            return fail(VK_CUDA_ERROR, "occupancy query for the planned decode kernel failed");
+        }
+    }
+    const int64_t cap = static_cast<int64_t>(pool->num_sms) * occ * kPlanWarps;
+    int64_t W = T > 0 ? std::min<int64_t>(cap, (T + kMinPagesPerWorker - 1) / kMinPagesPerWorker) : 0;
+    W = std::max<int64_t>(W, T > 0 ? 1 : 0);
+    pl->W = static_cast<int>(W);
+    const int zero_ctas = (pl->Z + kPlanWarps - 1) / kPlanWarps;
+    pl->grid = static_cast<int>(std::max<int64_t>((W + kPlanWarps - 1) / kPlanWarps, std::min<int64_t>(zero_ctas, cap / kPlanWarps)));
+    if (pl->grid == 0 && pl->Z > 0) pl->grid = 1;
+
+    // worker ranges and the unit each starts in
+    std::vector<int32_t> wb(static_cast<size_t>(W) + 1), wfu(static_cast<size_t>(W));
+    for (int64_t w = 0; w <= W; ++w) wb[w] = static_cast<int32_t>(W ? (w * T) / W : 0);
+    {
+        int u = 0;
+        for (int64_t w = 0; w < W; ++w) {
+            while (u < U && uoff[u + 1] <= wb[w]) ++u;
+            wfu[w] = u;
+        }
+    }
+    // pieces per unit
+    std::vector<int32_t> ufw(U, 0), unp(U, 0), uslot(U, -1);
+    auto worker_of = [&](int64_t g) {  // largest w with wb[w] <= g
+        int64_t lo = 0, hi = W - 1;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) / 2;
+            if (wb[mid] <= g) lo = mid; else hi = mid - 1;
+        }
+        return static_cast<int32_t>(lo);
+    };
+    int slots = 0;
+    for (int u = 0; u < U; ++u) {
+        if (uoff[u + 1] == uoff[u]) continue;
+        const int32_t f = worker_of(uoff[u]), l = worker_of(uoff[u + 1] - 1);
+        ufw[u] = f;
+        unp[u] = l - f + 1;
+        if (unp[u] > 1) {
+            uslot[u] = slots;
+            slots += unp[u];
+        }
+    }
+    pl->slots = slots;
+
+    // packed int32 tables
+    auto& t = pl->tables;
+    auto put = [&](const auto& v, size_t* off) {
+        *off = t.size();
+        for (auto x : v) t.push_back(static_cast<int32_t>(x));
+        while (t.size() % 64) t.push_back(0);  // keep each array 256-byte aligned
+    };
+    put(wb, &pl->o_wb);
+    put(wfu, &pl->o_wfu);
+    std::vector<int32_t> uoff32(uoff.begin(), uoff.end());
+    uoff32.push_back(uoff32.back() + 1);  // sentinel so the page iterator can run one unit past the end
+    put(uoff32, &pl->o_uoff);
+    put(ulen, &pl->o_ulen);
+    put(ufw, &pl->o_ufw);
+    put(unp, &pl->o_unp);
+    put(uslot, &pl->o_uslot);
+    put(zunits, &pl->o_z);
+    pl->tables_bytes = t.size() * sizeof(int32_t);
+    pl->counters_off = align256(pl->tables_bytes);
+    pl->part_o_off = align256(pl->counters_off + static_cast<size_t>(U) * sizeof(uint32_t));
+    pl->part_lse_off = align256(pl->part_o_off + static_cast<size_t>(slots) * G * D * sizeof(float));
+    pl->ws_bytes = align256(pl->part_lse_off + static_cast<size_t>(slots) * G * sizeof(float));
+    *out_plan = pl;
+    return VK_OK;
+}
+
+vk_status vk_decode_plan_destroy(vk_decode_plan* plan) {
+    delete plan;
+    return VK_OK;
+}
+
+size_t vk_decode_plan_workspace_size(const vk_decode_plan* plan) { return plan ? plan->ws_bytes : 0; }
+
+vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    if (!plan || !workspace || workspace_bytes < plan->ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(VK_INVALID_ARG, "workspace missing, too small or not 256-byte aligned");
+    DeviceGuard g(plan->device);
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e = cudaMemcpyAsync(workspace, plan->tables.data(), plan->tables_bytes, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(plan tables)");
+    if (plan->U > 0) {
+        e = cudaMemsetAsync(static_cast<char*>(workspace) + plan->counters_off, 0,
+                            static_cast<size_t>(plan->U) * sizeof(uint32_t), st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(plan counters)");
+    }
+    return VK_OK;
+}
+
+int32_t vk_decode_plan_info(const vk_decode_plan* plan, int32_t what) {
+    if (!plan) return -1;
+    switch (what) {
+        case 0: return plan->W;
+        case 1: return plan->grid;
+        case 2: return plan->slots;
+        case 3: return plan->total_pages;
+        case 4: return plan->max_unit_pages;
+        default: return -1;
+    }
+}
+
+vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer, const void* q, void* out,
+                        const int32_t* block_tables, int32_t bt_stride, const void* k_new, const void* v_new,
+                        float scale, void* workspace, void* stream) {
+    if (!pool || !plan) return fail(VK_INVALID_ARG, "pool or plan is NULL");
+    if (!pool->kv || !pool->tmap_ok) return fail(VK_UNSUPPORTED, "decode needs a KV pool addressable by TMA");
+    if (pool->cfg.head_dim != plan->D || pool->cfg.num_kv_heads != plan->Hkv || pool->device != plan->device)
+        return fail(VK_INVALID_ARG, "plan was made for another pool shape or device");
+    if (layer < 0 || layer >= pool->cfg.num_layers) return fail(VK_INVALID_ARG, "layer out of range");
+    if (plan->B == 0) return VK_OK;
+    if (!q || !out || !block_tables || !workspace) return fail(VK_INVALID_ARG, "NULL array");
+    if (bt_stride < plan->max_unit_pages) return fail(VK_INVALID_ARG, "block table narrower than the longest sequence");
+    if ((k_new == nullptr) != (v_new == nullptr)) return fail(VK_INVALID_ARG, "give both k_new and v_new or neither");
+    if (k_new && ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15))
+        return fail(VK_INVALID_ARG, "k_new/v_new must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(out) & 1) ||
+        (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(VK_INVALID_ARG, "misaligned q/out/workspace");
+    const int D = plan->D;
+    char* ws = static_cast<char*>(workspace);
+    PlanParams p;
+    const int32_t* t = reinterpret_cast<const int32_t*>(ws);
+    p.wb = t + plan->o_wb;
+    p.wfu = t + plan->o_wfu;
+    p.uoff = t + plan->o_uoff;
+    p.ulen = t + plan->o_ulen;
+    p.ufw = t + plan->o_ufw;
+    p.unp = t + plan->o_unp;
+    p.uslot = t + plan->o_uslot;
+    p.zunits = t + plan->o_z;
+    p.counters = reinterpret_cast<uint32_t*>(ws + plan->counters_off);
+    p.part_o = reinterpret_cast<float*>(ws + plan->part_o_off);
+    p.part_lse = reinterpret_cast<float*>(ws + plan->part_lse_off);
+    p.q = static_cast<const __half*>(q);
+    p.out = static_cast<__half*>(out);
+    p.k_new = static_cast<const __half*>(k_new);
+    p.v_new = static_cast<const __half*>(v_new);
+    p.bt = block_tables;
+    p.err = pool->d_err;
+    p.pool_base = pool->base;
+    p.seg_bytes = pool->seg_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
+    p.head_bytes = pool->head_bytes;
+    p.bt_stride = bt_stride;
+    p.Hq = plan->Hq;
+    p.Hkv = plan->Hkv;
+    p.G = plan->G;
+    p.L = pool->cfg.num_layers;
+    p.layer = layer;
+    p.num_pages = pool->num_pages;
+    p.W = plan->W;
+    p.Z = plan->Z;
+    const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
+    p.scale_log2 = sc * 1.4426950408889634f;
+    if (plan->grid <= 0) return VK_OK;
+    DeviceGuard g(pool->device);
+    cudaStream_t st = as_stream(stream);
+    int occ = 0;
+    if (occupancy_for(D, plan->NT, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
+    const dim3 grid(plan->grid), block(kPlanWarps * 32);
+#define VK_LAUNCH(DD, NN) \
+    planned_decode_kernel<DD, NN><<<grid, block, plan_smem_bytes<DD>(), st>>>(pool->tmap, p)
+    if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1); else VK_LAUNCH(128, 2); }
+    else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1); else VK_LAUNCH(64, 2); }
+    else { if (plan->NT == 1) VK_LAUNCH(256, 1); else VK_LAUNCH(256, 2); }
+#undef VK_LAUNCH
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "planned_decode_kernel launch");
+}
+
+}  // extern "C"

@@ -21,7 +21,6 @@ struct Allocator {
     // on the first word that may hold a free bit, so lowest-id allocation is
     // amortised O(1) and every id order matches a first-fit scan.
     std::vector<uint64_t> free_bits;
-    std::vector<uint8_t> swapped;  // an id whose contents were swapped out
     size_t hint = 0;
     int32_t num_pages = 0;
     int32_t used = 0;
@@ -41,9 +40,11 @@ struct vk_pool {
     bool owns_mem = false;
     int device = 0;
     char* base = nullptr;
-    uint64_t page_bytes = 0;
-    uint64_t layer_bytes = 0;
-    uint64_t head_bytes = 0;
+    uint64_t page_bytes = 0;   // bytes of one page over all its segments
+    uint64_t seg_bytes = 0;    // bytes of one page in one layer (the whole page for byte pools)
+    uint64_t seg_stride = 0;   // distance between a page's consecutive layer segments
+    int32_t nseg = 1;          // segments per page: num_layers (KV pools) or 1 (byte pools)
+    uint64_t head_bytes = 0;   // K block + V block of one (page, layer, head)
     int32_t num_pages = 0;
     uint32_t* d_err = nullptr;  // device error word (VK_ERR_* bits)
     alignas(64) CUtensorMap tmap;  // 2-D view: rows of head_dim fp16 over the whole pool

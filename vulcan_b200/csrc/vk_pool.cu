@@ -40,7 +40,6 @@ void Allocator::reset(int32_t n) {
     hint = 0;
     free_bits.assign((static_cast<size_t>(n) + 63) / 64, ~0ull);
     if (n % 64) free_bits.back() = (1ull << (n % 64)) - 1;
-    swapped.assign(static_cast<size_t>(n), 0);
 }
 
 int32_t Allocator::take_lowest() {
@@ -94,7 +93,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 // Rows of head_dim fp16 elements over the whole pool; a TMA box is 64 elements
 // (128 bytes, 128-byte swizzle) by 2*page_tokens rows: the K and V rows of one
-// (page, layer, head) for one 64-wide slice of the head dimension.
+// (layer, page, head) for one 64-wide slice of the head dimension.  The rows of
+// (layer, page, head) start at ((layer*num_pages + page)*Hkv + head)*2*page_tokens.
 static vk_status make_tmap(vk_pool* p) {
     const uint64_t rows =
         static_cast<uint64_t>(p->num_pages) * p->cfg.num_layers * p->cfg.num_kv_heads * 2 *
@@ -136,6 +136,22 @@ static vk_status check_cfg(const vk_pool_cfg* c, bool* kv, uint64_t* page_bytes)
     return VK_OK;
 }
 
+// Layer-major layout: segment `layer` of page `id` starts at
+// base + layer*seg_stride + id*seg_bytes, so one layer's pages form one
+// contiguous region of num_pages*seg_bytes.
+static void set_geometry(vk_pool* p) {
+    if (p->kv) {
+        p->head_bytes = 2ull * p->cfg.page_tokens * p->cfg.head_dim * 2;
+        p->seg_bytes = p->head_bytes * p->cfg.num_kv_heads;
+        p->nseg = p->cfg.num_layers;
+        p->seg_stride = p->seg_bytes * static_cast<uint64_t>(p->num_pages);
+    } else {
+        p->seg_bytes = p->page_bytes;
+        p->nseg = 1;
+        p->seg_stride = 0;
+    }
+}
+
 static vk_status finish_create(vk_pool* p, vk_pool** out) {
     cudaError_t e = cudaMalloc(&p->d_err, sizeof(uint32_t));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(error word)");
@@ -174,10 +190,7 @@ vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool) {
     p->device = cfg->device;
     p->page_bytes = pb;
     p->num_pages = cfg->num_pages;
-    if (kv) {
-        p->head_bytes = 2ull * cfg->page_tokens * cfg->head_dim * 2;
-        p->layer_bytes = p->head_bytes * cfg->num_kv_heads;
-    }
+    set_geometry(p);
     const uint64_t bytes = pb * static_cast<uint64_t>(cfg->num_pages);
     cudaError_t e = cudaMalloc(&p->base, bytes);
     if (e != cudaSuccess) {
@@ -221,10 +234,7 @@ vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t byt
     p->device = cfg->device;
     p->page_bytes = pb;
     p->num_pages = cfg->num_pages;
-    if (kv) {
-        p->head_bytes = 2ull * cfg->page_tokens * cfg->head_dim * 2;
-        p->layer_bytes = p->head_bytes * cfg->num_kv_heads;
-    }
+    set_geometry(p);
     p->base = static_cast<char*>(device_mem);
     p->owns_mem = false;
     s = finish_create(p, out_pool);
@@ -278,10 +288,7 @@ vk_status vk_alloc_pages(vk_pool* pool, int32_t n, int32_t* out_ids) {
         for (int32_t i = 0; i < n; ++i) out_ids[i] = -1;
         return fail(VK_OUT_OF_PAGES, "not enough free pages");
     }
-    for (int32_t i = 0; i < n; ++i) {
-        out_ids[i] = pool->alloc.take_lowest();
-        pool->alloc.swapped[out_ids[i]] = 0;
-    }
+    for (int32_t i = 0; i < n; ++i) out_ids[i] = pool->alloc.take_lowest();
     return VK_OK;
 }
 
@@ -291,14 +298,13 @@ vk_status vk_free_pages(vk_pool* pool, const int32_t* ids, int32_t n) {
         const int32_t id = ids[i];
         if (id < 0 || id >= pool->num_pages) continue;  // ignored, as the reference does
         pool->alloc.set_free(id);
-        pool->alloc.swapped[id] = 0;
     }
     return VK_OK;
 }
 
 void* vk_page_ptr(const vk_pool* pool, int32_t id) {
     if (!pool || id < 0 || id >= pool->num_pages) return nullptr;
-    return pool->base + static_cast<uint64_t>(id) * pool->page_bytes;
+    return pool->base + static_cast<uint64_t>(id) * pool->seg_bytes;
 }
 
 int32_t vk_pages_in_use(const vk_pool* pool) { return pool ? pool->alloc.used : 0; }
@@ -315,9 +321,25 @@ int32_t vk_page_in_use(const vk_pool* pool, int32_t id) {
 
 // ---------------------------------------------------------------- swap
 
-// Copies runs of consecutive ids with one cudaMemcpyAsync each.
+// Host buffers hold whole pages back to back (page i of the call at
+// host + i*page_bytes, its layer segments consecutive).  Byte pools copy runs of
+// consecutive ids with one cudaMemcpyAsync each; KV pools copy each page's
+// layer segments with one strided 2-D copy.
 static vk_status copy_runs(vk_pool* pool, const int32_t* ids, int32_t n, char* host, bool to_host,
                            cudaStream_t st) {
+    if (pool->nseg > 1) {
+        for (int32_t i = 0; i < n; ++i) {
+            char* dev = pool->base + static_cast<uint64_t>(ids[i]) * pool->seg_bytes;
+            char* h = host + static_cast<uint64_t>(i) * pool->page_bytes;
+            cudaError_t e =
+                to_host ? cudaMemcpy2DAsync(h, pool->seg_bytes, dev, pool->seg_stride, pool->seg_bytes, pool->nseg,
+                                            cudaMemcpyDeviceToHost, st)
+                        : cudaMemcpy2DAsync(dev, pool->seg_stride, h, pool->seg_bytes, pool->seg_bytes, pool->nseg,
+                                            cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync(swap)");
+        }
+        return VK_OK;
+    }
     int32_t i = 0;
     while (i < n) {
         int32_t j = i + 1;
@@ -345,10 +367,7 @@ vk_status vk_swap_out(vk_pool* pool, const int32_t* ids, int32_t n, void* host_b
     DeviceGuard g(pool->device);
     vk_status s = copy_runs(pool, ids, n, static_cast<char*>(host_buf), true, as_stream(stream));
     if (s != VK_OK) return s;
-    for (int32_t i = 0; i < n; ++i) {
-        pool->alloc.set_free(ids[i]);
-        pool->alloc.swapped[ids[i]] = 1;
-    }
+    for (int32_t i = 0; i < n; ++i) pool->alloc.set_free(ids[i]);
     return VK_OK;
 }
 
@@ -381,10 +400,7 @@ vk_status vk_swap_in_to(vk_pool* pool, const void* host_buf, const int32_t* ids,
     vk_status s = copy_runs(pool, ids, n, static_cast<char*>(const_cast<void*>(host_buf)), false,
                             as_stream(stream));
     if (s != VK_OK) return s;
-    for (int32_t i = 0; i < n; ++i) {
-        pool->alloc.set_used(ids[i]);
-        pool->alloc.swapped[ids[i]] = 0;
-    }
+    for (int32_t i = 0; i < n; ++i) pool->alloc.set_used(ids[i]);
     return VK_OK;
 }
 

@@ -60,10 +60,11 @@ def _need(t: torch.Tensor, dtype, name: str, device=True):
 class PagedKVPool:
     """A paged fp16 KV pool for ``num_layers`` layers and ``num_kv_heads`` heads.
 
-    Memory layout per page (see include/vk_paged_kv.h):
-    ``[num_layers, num_kv_heads, 2 (K,V), page_tokens, head_dim]`` fp16.  The
-    pool storage is a torch allocation handed to the library
-    (``vk_pool_create_in``) unless ``own_memory`` is set.
+    Layer-major fp16 layout (see include/vk_paged_kv.h):
+    ``[num_layers, num_pages, num_kv_heads, 2 (K,V), page_tokens, head_dim]``,
+    so one layer's pages form one contiguous region.  The pool storage is a
+    torch allocation handed to the library (``vk_pool_create_in``) unless
+    ``own_memory`` is set.
     """
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_pages: int,
@@ -95,10 +96,10 @@ class PagedKVPool:
 
     # ------------------------------------------------------------------ views
     def kv_view(self) -> torch.Tensor:
-        """fp16 view [num_pages, L, Hkv, 2, page_tokens, head_dim] of the pool."""
+        """fp16 view [L, num_pages, Hkv, 2, page_tokens, head_dim] of the pool."""
         if self.storage is None or not self.kv:
             raise RuntimeError("kv_view needs a torch-backed KV pool")
-        return self.storage.view(torch.float16).view(self.num_pages, self.num_layers, self.num_kv_heads,
+        return self.storage.view(torch.float16).view(self.num_layers, self.num_pages, self.num_kv_heads,
                                                      2, self.page_tokens, self.head_dim)
 
     @property
@@ -194,6 +195,11 @@ class PagedKVPool:
                                   _ptr(workspace), ws_bytes, _stream(stream)), "vk_decode")
         return out
 
+    def plan(self, seq_lens: Sequence[int], num_q_heads: int,
+             workspace: Optional[torch.Tensor] = None) -> "DecodePlan":
+        """Host-side balanced schedule for one decode step (lengths include the new token)."""
+        return DecodePlan(self, seq_lens, num_q_heads, workspace)
+
     def prefill(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor, positions: torch.Tensor,
                 out: Optional[torch.Tensor] = None, scale: float = 0.0, stream=None) -> torch.Tensor:
         """q: [B, T, Hq, D] fp16; positions [B] int32 (chunk start); returns [B, T, Hq, D] fp16."""
@@ -241,6 +247,73 @@ class PagedKVPool:
             self._lib.vk_pool_destroy(self.handle)
             self.handle = ctypes.c_void_p()
         self.storage = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DecodePlan:
+    """vk_decode_plan: built on the host from the step's lengths, uploaded once
+    into a device workspace, then run once per layer (vk_decode_run)."""
+
+    def __init__(self, pool: PagedKVPool, seq_lens: Sequence[int], num_q_heads: int,
+                 workspace: Optional[torch.Tensor] = None):
+        self.pool = pool
+        self._lib = pool._lib
+        lens = [int(x) for x in seq_lens]
+        self.batch, self.num_q_heads = len(lens), num_q_heads
+        h = ctypes.c_void_p()
+        check(self._lib.vk_decode_plan_create(pool.handle, _i32_array(lens), len(lens), num_q_heads,
+                                              ctypes.byref(h)), "vk_decode_plan_create")
+        self.handle = h
+        nbytes = max(256, self._lib.vk_decode_plan_workspace_size(h))
+        if workspace is not None and workspace.numel() >= nbytes and workspace.data_ptr() % 256 == 0:
+            self.workspace = workspace
+        else:
+            self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=pool.device)
+        self.uploaded = False
+
+    def info(self, what: int) -> int:
+        return self._lib.vk_decode_plan_info(self.handle, what)
+
+    @property
+    def workers(self) -> int:
+        return self.info(0)
+
+    @property
+    def ctas(self) -> int:
+        return self.info(1)
+
+    def upload(self, stream=None) -> None:
+        check(self._lib.vk_decode_plan_upload(self.handle, _ptr(self.workspace), self.workspace.numel(),
+                                              _stream(stream)), "vk_decode_plan_upload")
+        self.uploaded = True
+
+    def run(self, layer: int, q: torch.Tensor, block_tables: torch.Tensor, out: Optional[torch.Tensor] = None,
+            k_new: Optional[torch.Tensor] = None, v_new: Optional[torch.Tensor] = None, scale: float = 0.0,
+            stream=None) -> torch.Tensor:
+        """q [B, Hq, D] fp16; optional k_new/v_new [B, Hkv, D] fp16 appended at position len-1."""
+        if not self.uploaded:
+            self.upload(stream)
+        _need(q, torch.float16, "q")
+        _need(block_tables, torch.int32, "block_tables")
+        if k_new is not None:
+            _need(k_new, torch.float16, "k_new")
+            _need(v_new, torch.float16, "v_new")
+        if out is None:
+            out = torch.empty_like(q)
+        check(self._lib.vk_decode_run(self.pool.handle, self.handle, layer, _ptr(q), _ptr(out), _ptr(block_tables),
+                                      block_tables.shape[1], _ptr(k_new), _ptr(v_new), float(scale),
+                                      _ptr(self.workspace), _stream(stream)), "vk_decode_run")
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self._lib.vk_decode_plan_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
 
     def __del__(self):
         try:
@@ -362,13 +435,13 @@ class KVCache:
         self._current_len = max(self._current_len, start_pos + num_tokens)
 
     def get(self, layer: int):
-        """Pool addresses of this layer's K and V blocks of physical page 0; the
-        element at (page, kv head, slot, d) of layer ``layer`` is at
-        ``k + page*page_bytes + head*2*P*D*2 + (slot*D + d)*2`` (V: ``v`` + same)."""
+        """Device addresses of this layer's K and V blocks of physical page 0;
+        the element (page, kv head, slot, d) of the layer is at
+        ``k + (page*Hkv + head)*2*P*D*2 + (slot*D + d)*2`` (V: same from ``v``)."""
         if layer < 0 or layer >= self._num_layers:
             return None, None
-        base = self.pool.base_ptr
-        k = base + layer * self._num_kv_heads * 2 * PAGE_TOKENS * self._head_dim * 2
+        seg = self._num_kv_heads * 2 * PAGE_TOKENS * self._head_dim * 2
+        k = self.pool.base_ptr + layer * seg * self.pool.num_pages
         return k, k + PAGE_TOKENS * self._head_dim * 2
 
     def decode(self, layer: int, q: torch.Tensor, num_q_heads: Optional[int] = None) -> torch.Tensor:
