@@ -50,6 +50,15 @@ def workload(name: str):
                     desc="Llama-2-70B GQA decode: B=64, Hq=64, Hkv=8, D=128, L=80, 16-token pages, "
                          "ctx lognormal(median 2048, sigma 0.6) clipped [256, 8192], random block table",
                     sigma=sigma, seed=2048)
+    if name == "prefill":
+        rng = np.random.Generator(np.random.PCG64(8192))
+        B = 8
+        ctx = rng.integers(0, 4097, B).astype(np.int64)  # cached prefix before the chunk
+        return dict(name="llama2-7b-chunked-prefill", B=B, Hq=32, Hkv=32, D=128, L=32, T=2048, ctx=ctx,
+                    shard="seq",
+                    desc="Llama-2-7B chunked prefill: 8 sequences x 2048-token chunk appended into 16-token "
+                         "pages over cached prefixes U[0, 4096], Hq=Hkv=32, D=128, L=32, random block table",
+                    seed=8192)
     if name == "7b":
         rng = np.random.Generator(np.random.PCG64(4096))
         B = 32
@@ -219,7 +228,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="70b", choices=["70b", "7b"])
+    ap.add_argument("--config", default="70b", choices=["70b", "7b", "prefill"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -243,6 +252,8 @@ def main():
         wl["desc"] += " [profiling case: first %d sequences]" % args.batch
     if args.impl == "reference":
         return run_reference_arm(args, wl)
+    if args.config == "prefill":
+        return run_prefill(args, wl)
 
     import torch
     import torch.distributed as dist
@@ -469,6 +480,113 @@ def main():
             "cpu_baseline": cpu,
             "e2e": e2e,
         }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def prefill_flops(ctx, T, Hq, D):
+    """Attention FLOPs of one layer: QK^T and PV, 2 FLOPs per multiply-add, over
+    the causal (query, key) pairs of each chunk (prefix keys + lower triangle)."""
+    pairs = sum(int(T * c + T * (T + 1) // 2) for c in ctx)
+    return 4 * D * Hq * pairs
+
+
+def run_prefill(args, wl):
+    """Config 4: per layer, append the 2048-token chunks (K1) then causal prefill
+    attention over prefix + chunk (K3); one CUDA graph per step of L layers.
+    Sequences are sharded over ranks (no collective)."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    import vulcan_b200 as vk
+    B, H, D, L, T = wl["B"], wl["Hq"], wl["D"], wl["L"], wl["T"]
+    seqs = np.arange(B)[rank::world]
+    ctx = wl["ctx"][seqs]
+    Bl = len(seqs)
+    bt, num_pages = layout(ctx + T - 1, wl["seed"] + rank, slack=1.0)
+    pool = vk.PagedKVPool(L, H, D, num_pages, zero=False)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5 + rank)
+    flat = pool.storage.view(torch.float16)
+    for s0 in range(0, flat.numel(), 1 << 28):
+        part = flat[s0:s0 + (1 << 28)]
+        part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    bt_d = torch.from_numpy(bt).to(dev)
+    pos_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    q = (torch.randn(Bl, T, H, D, device=dev, generator=gen) * 0.5).half()
+    kn = (torch.randn(Bl, T, H, D, device=dev, generator=gen) * 0.5).half()
+    vn = (torch.randn(Bl, T, H, D, device=dev, generator=gen) * 0.5).half()
+    out = torch.empty_like(q)
+    compute = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+          for _ in range(L)]
+
+    def layers(record):
+        cur = torch.cuda.current_stream(dev)
+        for l in range(L):
+            pool.append(l, kn, vn, bt_d, pos_d)
+            if record:
+                ev[l][0].record(cur)
+            pool.prefill(l, q, bt_d, pos_d, out=out)
+            if record:
+                ev[l][1].record(cur)
+
+    for _ in range(args.warmup):
+        layers(False)
+    pool.check()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(compute)
+    with torch.cuda.graph(graph, stream=cap):
+        layers(True)
+    compute.wait_stream(cap)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t0.record(compute)
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record(compute)
+        torch.cuda.synchronize(dev)
+    pool.check()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    launch_ms = sum(a.elapsed_time(b) for a, b in ev) / L
+    flops_local = prefill_flops(ctx, T, H, D)
+    flops_job = prefill_flops(wl["ctx"], T, H, D)
+    peak_t = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    achieved = flops_local / (launch_ms * 1e-3) / 1e12
+    if rank == 0:
+        line = {"metric": "chunked prefill (append + causal attention) tokens/s and TFLOP/s",
+                "value": B * T / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.5^2) fp16)",
+                "config": {"workload": wl["desc"], "launch": "CUDA graph of the %d-layer step" % L,
+                           "shard": "sequence x%d" % world if world > 1 else "none"},
+                "attn_tflops": flops_job * L / (ms_step * 1e-3) / 1e12,
+                "gpu_launches": 2 * L * args.steps, "clocks": clk.summary(),
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
+                             "frac": achieved / peak_t, "traffic": None, "kernel": "vk_prefill",
+                             "launch_ms": launch_ms, "flops_per_launch": flops_local}}
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
