@@ -31,6 +31,7 @@ import sys
 import time
 
 import numpy as np
+from typing import List
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -59,6 +60,15 @@ def workload(name: str):
                     desc="Llama-2-7B chunked prefill: 8 sequences x 2048-token chunk appended into 16-token "
                          "pages over cached prefixes U[0, 4096], Hq=Hkv=32, D=128, L=32, random block table",
                     seed=8192)
+    if name == "churn":
+        rng = np.random.Generator(np.random.PCG64(32768))
+        B = 256
+        ctx = rng.integers(1024, 32769, B).astype(np.int64)
+        return dict(name="long-context-churn", B=B, Hq=32, Hkv=32, D=128, L=1, ctx=ctx, shard="seq",
+                    rate=16, steps=200, capacity=0.7, seed=32768,
+                    desc="Long-context paged churn, Llama-2-7B head shapes (32/32, D=128), 1 layer: 256 "
+                         "sequences arriving Poisson(16)/step, contexts U[1k, 32k], pool 70% of demand, "
+                         "LRU swap to pinned host and back, compaction by page copy every 25 steps, 200 decode steps")
     if name == "7b":
         rng = np.random.Generator(np.random.PCG64(4096))
         B = 32
@@ -228,7 +238,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="70b", choices=["70b", "7b", "prefill"])
+    ap.add_argument("--config", default="70b", choices=["70b", "7b", "prefill", "churn"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -237,6 +247,8 @@ def main():
                          "split: vk_append + vk_decode (split grid + merge kernel)")
     ap.add_argument("--pps", type=int, default=0, help="override decode pages per split (0 = auto)")
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph")
+    ap.add_argument("--no-early-start", action="store_true",
+                    help="launch each layer's decode only after the previous one completes")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
     ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
     args = ap.parse_args()
@@ -254,6 +266,8 @@ def main():
         return run_reference_arm(args, wl)
     if args.config == "prefill":
         return run_prefill(args, wl)
+    if args.config == "churn":
+        return run_churn(args, wl)
 
     import torch
     import torch.distributed as dist
@@ -274,22 +288,14 @@ def main():
     B, Hq, Hkv, D, L = wl["B"], wl["Hq"], wl["Hkv"], wl["D"], wl["L"]
     ctx_all = wl["ctx"]
     bt_all, num_pages_all = layout(ctx_all, wl["seed"])
+    from vulcan_b200.shard import head_shard, seq_shard
     if wl["shard"] == "head":
-        if Hkv % world:
-            raise SystemExit("KV heads %d not divisible by %d GPUs" % (Hkv, world))
-        hkv_l, hq_l = Hkv // world, Hq // world
+        sh = head_shard(Hkv, Hq, world, rank)
+        hkv_l, hq_l = sh.num_kv_heads, sh.num_q_heads
         seqs = np.arange(B)
         ctx, bt, num_pages = ctx_all, bt_all, num_pages_all
     else:
-        # sequence sharding balanced by tokens: greedy longest-first onto the least-loaded rank
-        order = np.argsort(-ctx_all, kind="stable")
-        loads = [0] * world
-        owner = np.zeros(B, np.int64)
-        for i in order:
-            r = int(np.argmin(loads))
-            owner[i] = r
-            loads[r] += int(ctx_all[i] + 1)
-        seqs = np.nonzero(owner == rank)[0]
+        seqs = seq_shard(ctx_all + 1, world)[rank]
         hkv_l, hq_l = Hkv, Hq
         ctx = ctx_all[seqs]
         bt, num_pages = layout(ctx, wl["seed"] + 17 * rank)
@@ -329,13 +335,15 @@ def main():
     merge_launched = 1 if pool.workspace_size(Bl, hq_l, max_len) > 0 else 0
     launches_per_step = L * (2 + merge_launched) if args.path == "split" else L
 
-    use_graph = world == 1 and not args.eager
+    use_graph = not args.eager
     plan_keep = {}
 
     def new_plan():
         """Host plan for this step (every layer shares the lengths), uploaded in stream order."""
         if args.path == "planned":
             p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+            if not args.no_early_start:
+                p_.set_early_start(True)  # layers are back to back: overlap each launch's start
             p_.upload()
             plan_keep["plan"] = p_
 
@@ -375,6 +383,7 @@ def main():
     barrier()
 
     graph = None
+    per_layer_events = True
     if use_graph:
         # the whole L-layer step as one CUDA graph; timing events are graph nodes
         layer_events = [(torch.cuda.Event(enable_timing=True, external=True),
@@ -382,8 +391,11 @@ def main():
         graph = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream(device=dev)
         cap.wait_stream(compute)
+        # Event nodes between launches would break the early-start edges; with
+        # early start the per-launch time is the step time over the layers.
+        per_layer_events = args.path == "split" or args.no_early_start
         with torch.cuda.graph(graph, stream=cap):
-            layers(layer_events)
+            layers(layer_events if per_layer_events else None)
         compute.wait_stream(cap)
         new_plan()
         graph.replay()
@@ -415,13 +427,15 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
     ms_step = ms_total / args.steps
-    try:  # per-launch durations of the last timed step
-        dec_ms = [a.elapsed_time(b) for a, b in layer_events]
-        dec_avg_ms = sum(dec_ms) / len(dec_ms)
-        dec_src = "CUDA events around each decode launch of the last timed step"
-    except RuntimeError:
-        dec_avg_ms = ms_step / L
-        dec_src = "step time / layers (events unavailable)"
+    dec_avg_ms = ms_step / L
+    dec_src = "step time / layers (launches back to back, early start)"
+    if not use_graph or per_layer_events:
+        try:  # per-launch durations of the last timed step
+            dec_ms = [a.elapsed_time(b) for a, b in layer_events]
+            dec_avg_ms = sum(dec_ms) / len(dec_ms)
+            dec_src = "CUDA events around each decode launch of the last timed step"
+        except RuntimeError:
+            dec_src = "step time / layers (events unavailable)"
     clocks = clk.summary()
 
     # --- algorithmic bytes (this rank's share) and roofline of the decode launch
@@ -485,6 +499,140 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_churn(args, wl):
+    """Config 5 on one GPU through vulcan_b200.scheduler: arrivals, LRU swap-out
+    to a pinned host arena, swap-in, one decode launch per step (planned, fused
+    append) over the resident sequences, compaction by page copy.  Swaps run on a
+    side stream and are timed with CUDA events on it; decode and copies on the
+    compute stream."""
+    import torch
+    import vulcan_b200 as vk
+    from vulcan_b200.scheduler import PagedKVScheduler
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    H, D, steps = wl["Hq"], wl["D"], wl["steps"]
+    ctx = wl["ctx"]
+    need = int(((ctx + steps + 15) // 16).sum())
+    num_pages = int(wl["capacity"] * need)
+    pool = vk.PagedKVPool(1, H, D, num_pages, zero=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    flat = pool.storage.view(torch.float16)
+    for s0 in range(0, flat.numel(), 1 << 28):
+        part = flat[s0:s0 + (1 << 28)]
+        part.copy_(torch.randn(part.shape, device=dev, generator=g) * 0.5)
+    host_slots = need - num_pages + 2048
+    host = torch.empty(host_slots * pool.page_bytes, dtype=torch.uint8, pin_memory=True)
+    swap_stream = torch.cuda.Stream(device=dev)
+    compute = torch.cuda.current_stream(dev)
+    swap_events = {"out": [], "in": []}
+
+    def on_swap(kind, pages, fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        swap_stream.wait_stream(compute)  # pages leaving were last written on the compute stream
+        e0.record(swap_stream)
+        r = fn()
+        e1.record(swap_stream)
+        swap_events[kind].append((e0, e1, pages))
+        return r
+
+    sched = PagedKVScheduler(pool, host_buffer=host, host_slots=host_slots, swap_stream=swap_stream,
+                             on_swap=on_swap)
+    rng = np.random.Generator(np.random.PCG64(wl["seed"] + 1))
+    arrivals = rng.poisson(wl["rate"], steps)
+    kq = (torch.randn(wl["B"], H, D, device=dev, generator=g) * 0.5).half()
+    kn = (torch.randn(wl["B"], H, D, device=dev, generator=g) * 0.5).half()
+    plan_ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+    copy_events = []
+    dec_events = []
+    decoded = 0
+    dec_bytes = 0
+    next_sid = 0
+    pending: List[int] = []
+
+    def copy_fn(src, dst):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        src_d = torch.tensor(src, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        dst_d = torch.tensor(dst, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        e0.record(compute)
+        pool.copy_pages(src_d, dst_d)
+        e1.record(compute)
+        copy_events.append((e0, e1, len(src)))
+
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    wall0 = time.perf_counter()
+    t0.record(compute)
+    for step in range(steps):
+        for _ in range(int(arrivals[step])):
+            if next_sid < wl["B"]:
+                pending.append(next_sid)
+                next_sid += 1
+        protect = set()
+        for _ in range(4):  # bring back the longest-waiting swapped sequences
+            if not sched.swapped:
+                break
+            sid = next(iter(sched.swapped))
+            if not sched.restore(sid, protect=protect):
+                break
+            protect.add(sid)
+        while pending:
+            sid = pending[0]
+            if not sched.admit(sid, int(ctx[sid])):
+                break
+            pending.pop(0)
+            protect.add(sid)
+        active = sched.resident_ids()
+        active = [sid for sid in active if sched.grow(sid, protect=protect)]
+        active = [sid for sid in active if sched.seqs[sid].resident]
+        if step % 25 == 24:
+            compute.wait_stream(swap_stream)
+            sched.compact(copy_fn=copy_fn)
+        if not active:
+            continue
+        bt = torch.from_numpy(sched.block_table(active)).to(dev, non_blocking=True)
+        lens = sched.lengths(active)
+        compute.wait_stream(swap_stream)  # restored pages in, evicted pages out
+        plan = pool.plan(lens.tolist(), H, workspace=plan_ws)
+        plan.upload()
+        idx = torch.tensor(active, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(compute)
+        plan.run(0, kq[idx], bt, k_new=kn[idx], v_new=kn[idx])
+        e1.record(compute)
+        dec_events.append((e0, e1))
+        decoded += len(active)
+        dec_bytes += algorithmic_bytes(lens.astype(np.int64) - 1, H, H, D)["total"]
+    compute.wait_stream(swap_stream)
+    t1.record(compute)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - wall0
+    pool.check()
+    ms = t0.elapsed_time(t1)
+    dec_ms = sum(a.elapsed_time(b) for a, b in dec_events)
+    res = {"metric": "long-context churn: decode tokens/s and swap / copy GB/s", "value": decoded / (ms * 1e-3),
+           "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": 0, "ms_per_step": ms / steps,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+           "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "pool_pages": num_pages,
+                                                   "demand_pages": need, "host_slots": host_slots,
+                                                   "page_bytes": pool.page_bytes},
+           "decode": {"tokens": decoded, "ms": dec_ms, "hbm_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9},
+           "wall_s": wall}
+    for kind in ("out", "in"):
+        ev = swap_events[kind]
+        tms = sum(a.elapsed_time(b) for a, b, _ in ev)
+        byt = sum(n for _, _, n in ev) * pool.page_bytes
+        res["swap_" + kind] = {"calls": len(ev), "bytes": byt, "ms": tms,
+                               "gbs": byt / (tms * 1e-3) / 1e9 if tms > 0 else None}
+    cms = sum(a.elapsed_time(b) for a, b, _ in copy_events)
+    cby = sum(n for _, _, n in copy_events) * pool.page_bytes * 2
+    res["copy"] = {"calls": len(copy_events), "pages": sum(n for _, _, n in copy_events), "ms": cms,
+                   "gbs_read_plus_write": cby / (cms * 1e-3) / 1e9 if cms > 0 else None}
+    res["scheduler"] = dict(sched.stats)
+    print(json.dumps(res), flush=True)
 
 
 def prefill_flops(ctx, T, Hq, D):
@@ -696,6 +844,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
         layers()
     barrier()
     graph = None
+    per_layer_events = True
     if use_graph:
         graph = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream(device=dev)

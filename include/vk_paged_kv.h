@@ -189,6 +189,15 @@ size_t    vk_decode_plan_workspace_size(const vk_decode_plan* plan);
  * merge counters, asynchronously on `stream`. */
 vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace,
                                 size_t workspace_bytes, void* stream);
+/* Early start (programmatic dependent launch): when enabled, vk_decode_run's
+ * grid may begin while the preceding kernel on the stream is still running; it
+ * reads the plan tables, block tables and pool pages early, and waits for that
+ * kernel to finish before it reads q, k_new, v_new or writes out and the merge
+ * scratch.  Enable only when the preceding kernel writes none of the block
+ * tables or pool pages this run reads (for example back-to-back layers of one
+ * step).  Default off. */
+vk_status vk_decode_plan_set_early_start(vk_decode_plan* plan, int32_t enable);
+
 /* Plan facts: 0 workers, 1 CTAs, 2 partial slots, 3 total pages, 4 longest
  * sequence in pages; -1 for an unknown query. */
 int32_t   vk_decode_plan_info(const vk_decode_plan* plan, int32_t what);

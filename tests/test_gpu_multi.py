@@ -1,0 +1,99 @@
+"""Two-GPU test of KV-head-sharded decode with the NCCL all-gather: each rank
+holds half of the KV heads of a 70B-shaped pool, decodes its query heads with
+the planned kernel (fused append), and the all-gathered output matches a
+single-GPU decode of the full pool within the attention tolerance.  Skipped
+when fewer than two GPUs are visible.  Child processes, NVLS off, short
+process-group timeout."""
+import datetime
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _data():
+    from tests.helpers import random_layout
+    import oracle
+    rng = np.random.default_rng(2)
+    B, Hq, Hkv, D, L = 16, 64, 8, 128, 2
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(2048), 0.6, B))), 256, 8192).astype(np.int32) + 1
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool = (rng.standard_normal(g.pool_shape(), dtype=np.float32) * 0.5).astype(np.float16)
+    q = (rng.standard_normal((B, Hq, D)) * 0.5).astype(np.float16)
+    kn = (rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16)
+    vn = (rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16)
+    return g, bt, lens, pool, q, kn, vn, Hq
+
+
+def _worker(rank, world, port, results):
+    import sys
+    sys.path.insert(0, ROOT)
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        import torch.distributed as dist
+        import vulcan_b200 as vk
+        from vulcan_b200.shard import gathered_to_heads, head_shard
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        g, bt, lens, pool, q, kn, vn, Hq = _data()
+        sh = head_shard(g.Hkv, Hq, world, rank)
+        lp = vk.PagedKVPool(g.L, sh.num_kv_heads, g.D, g.num_pages)
+        lp.kv_view().copy_(torch.from_numpy(np.ascontiguousarray(pool[:, :, sh.kv_lo:sh.kv_hi])).view(torch.float16))
+        bt_d = torch.from_numpy(bt).to(dev)
+        plan = lp.plan(lens.tolist(), sh.num_q_heads)
+        out = plan.run(1, torch.from_numpy(np.ascontiguousarray(q[:, sh.q_lo:sh.q_hi])).to(dev), bt_d,
+                       k_new=torch.from_numpy(np.ascontiguousarray(kn[:, sh.kv_lo:sh.kv_hi])).to(dev),
+                       v_new=torch.from_numpy(np.ascontiguousarray(vn[:, sh.kv_lo:sh.kv_hi])).to(dev))
+        gathered = torch.empty(world, *out.shape, dtype=out.dtype, device=dev)
+        dist.all_gather_into_tensor(gathered.view(-1), out.contiguous().view(-1))
+        full = gathered_to_heads(gathered).float().cpu()
+        lp.check()
+        ok = True
+        if rank == 0:  # single-GPU reference on the whole pool
+            fp = vk.PagedKVPool(g.L, g.Hkv, g.D, g.num_pages)
+            fp.kv_view().copy_(torch.from_numpy(pool).view(torch.float16))
+            ref = fp.plan(lens.tolist(), Hq).run(1, torch.from_numpy(q).to(dev), bt_d,
+                                                 k_new=torch.from_numpy(kn).to(dev),
+                                                 v_new=torch.from_numpy(vn).to(dev)).float().cpu()
+            err = (full - ref).abs()
+            ok = bool((err <= 2e-3 + 1e-2 * ref.abs()).all())
+        results[rank] = ok
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        results[rank] = "exception: " + traceback.format_exc(limit=3)
+
+
+def test_head_sharded_decode_two_gpus(cuda_ok):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert dict(results) == {0: True, 1: True}, dict(results)

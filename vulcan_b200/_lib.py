@@ -58,6 +58,7 @@ SIGNATURES = {
     "vk_decode_plan_workspace_size": (c_sz, [vp]),
     "vk_decode_plan_upload": (c_i32, [vp, vp, c_sz, vp]),
     "vk_decode_plan_info": (c_i32, [vp, c_i32]),
+    "vk_decode_plan_set_early_start": (c_i32, [vp, c_i32]),
     "vk_decode_run": (c_i32, [vp, vp, c_i32, vp, vp, vp, c_i32, vp, vp, c_f32, vp, vp]),
     "vk_set_decode_split": (c_i32, [vp, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),

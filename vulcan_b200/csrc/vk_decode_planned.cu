@@ -62,8 +62,25 @@ __host__ __device__ constexpr int plan_smem_bytes() {
     return kPlanWarps * kPlanStages * (2 * kPageTokens * D * 2) + kPlanWarps * kPlanStages * 8 + 1024;
 }
 
+// Programmatic dependent launch: let the next kernel on the stream start
+// launching, and wait for the previous one to complete (no-ops when the launch
+// did not opt in).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Writes zeros for a unit without pages (a sequence of length 0).
+template <int D>
+__device__ __forceinline__ void zero_unit(const PlanParams& p, int u, int lane) {
+    __half* o = p.out + (static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G) * D;
+    for (int e = lane; e < p.G * D; e += 32) o[e] = __float2half(0.f);
 }
 
 // Iterator over (unit, page-in-unit) along the concatenated page list.
@@ -155,22 +172,23 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int w = blockIdx.x * kPlanWarps + warp;
 
-    // Units without pages: zero output (spread over all warps of the grid).
-    for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
-        const int u = p.zunits[i];
-        __half* o = p.out + (static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G) * D;
-        for (int e = lane; e < p.G * D; e += 32) o[e] = __float2half(0.f);
-    }
+    griddep_launch_dependents();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPlanWarps * NS; ++s) mbar_init(smem_u32(&bars[s]), 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (w >= p.W) return;
-    const int g0 = p.wb[w];
-    const int n = p.wb[w + 1] - g0;
-    if (n <= 0) return;
+    // Before griddep_wait only the plan tables, block tables and pool pages are
+    // read (not written by the preceding kernel); q, k_new, v_new, out and the
+    // merge scratch are touched after it.
+    const int g0 = w < p.W ? p.wb[w] : 0;
+    const int n = w < p.W ? p.wb[w + 1] - g0 : 0;
+    if (n <= 0) {
+        griddep_wait();
+        for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) zero_unit<D>(p, p.zunits[i], lane);
+        return;
+    }
 
     uint8_t* my_stages = smem + warp * NS * SB;
     uint64_t* full = bars + warp * NS;
@@ -214,8 +232,13 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
         pf.next(p.uoff);
     };
 
+    // Prefetch the first stages; a unit's last page waits for k_new/v_new.
     const int pre = min(n, NS);
-    for (int j = 0; j < pre; ++j) issue(j);
+    int issued = 0;
+    while (issued < pre && !(p.k_new != nullptr && pf.p == pf.np - 1)) issue(issued++);
+    griddep_wait();
+    while (issued < pre) issue(issued++);
+    for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) zero_unit<D>(p, p.zunits[i], lane);
 
     uint32_t qf[NT][KS][2];
     WarpSoftmaxState<D, NT> st;
@@ -341,6 +364,7 @@ struct vk_decode_plan {
     std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_z = 0;
     size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
+    bool early_start = false;
 };
 
 using namespace vk;
@@ -490,6 +514,12 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, siz
     return VK_OK;
 }
 
+vk_status vk_decode_plan_set_early_start(vk_decode_plan* plan, int32_t enable) {
+    if (!plan) return fail(VK_INVALID_ARG, "plan is NULL");
+    plan->early_start = enable != 0;
+    return VK_OK;
+}
+
 int32_t vk_decode_plan_info(const vk_decode_plan* plan, int32_t what) {
     if (!plan) return -1;
     switch (what) {
@@ -561,12 +591,26 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     int occ = 0;
     if (occupancy_for(D, plan->NT, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
     const dim3 grid(plan->grid), block(kPlanWarps * 32);
-#define VK_LAUNCH(DD, NN) \
-    planned_decode_kernel<DD, NN><<<grid, block, plan_smem_bytes<DD>(), st>>>(pool->tmap, p)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = plan->early_start ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le = cudaSuccess;
+#define VK_LAUNCH(DD, NN)                                                                   \
+    do {                                                                                    \
+        cfg.dynamicSmemBytes = plan_smem_bytes<DD>();                                       \
+        le = cudaLaunchKernelEx(&cfg, planned_decode_kernel<DD, NN>, pool->tmap, p);        \
+    } while (0)
     if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1); else VK_LAUNCH(128, 2); }
     else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1); else VK_LAUNCH(64, 2); }
     else { if (plan->NT == 1) VK_LAUNCH(256, 1); else VK_LAUNCH(256, 2); }
 #undef VK_LAUNCH
+    if (le != cudaSuccess) return cuda_fail(le, "planned_decode_kernel launch");
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "planned_decode_kernel launch");
 }

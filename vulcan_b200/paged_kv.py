@@ -279,6 +279,11 @@ class DecodePlan:
     def info(self, what: int) -> int:
         return self._lib.vk_decode_plan_info(self.handle, what)
 
+    def set_early_start(self, enable: bool = True) -> None:
+        """Programmatic dependent launch for back-to-back runs (see the C header)."""
+        check(self._lib.vk_decode_plan_set_early_start(self.handle, int(bool(enable))),
+              "vk_decode_plan_set_early_start")
+
     @property
     def workers(self) -> int:
         return self.info(0)
