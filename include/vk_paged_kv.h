@@ -217,6 +217,12 @@ vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, void* out,
                      const int32_t* positions, int32_t batch, int32_t tokens,
                      int32_t num_q_heads, float scale, void* stream);
 
+/* Selects the prefill kernel for the pool: 0 = automatic (the tcgen05/TMEM
+ * kernel for head_dim 128, the mma.sync kernel otherwise), 1 = the mma.sync
+ * kernel, 2 = the tcgen05 kernel (VK_UNSUPPORTED from vk_prefill for other
+ * head dims). */
+vk_status vk_set_prefill_path(vk_pool* pool, int32_t path);
+
 /* ---- K4: page copy (fork / compaction; no reference counterpart) -----------
  * dst_ids[i] <- src_ids[i] byte-exactly, whole pages, every layer.  Both are
  * int32 device arrays of n ids; no id may appear in both arrays. */

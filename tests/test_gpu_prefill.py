@@ -19,7 +19,7 @@ def vk(cuda_ok):
     return vulcan_b200
 
 
-def _run(vk, rng, D, Hq, Hkv, T, pos, poison=False, L=2, layer=1):
+def _run(vk, rng, D, Hq, Hkv, T, pos, poison=False, L=2, layer=1, path=0):
     pos = np.array(pos, np.int32)
     B = len(pos)
     g = oracle.Geom(L, Hkv, D, 16, 0)
@@ -32,6 +32,7 @@ def _run(vk, rng, D, Hq, Hkv, T, pos, poison=False, L=2, layer=1):
     else:
         host = random_pool(rng, g)
     pool = make_pool(vk, g, host)
+    pool.set_prefill_path(path)
     k = (rng.standard_normal((B, T, Hkv, D)) * 0.5).astype(np.float16)
     v = (rng.standard_normal((B, T, Hkv, D)) * 0.5).astype(np.float16)
     q = (rng.standard_normal((B, T, Hq, D)) * 0.5).astype(np.float16)
@@ -44,26 +45,42 @@ def _run(vk, rng, D, Hq, Hkv, T, pos, poison=False, L=2, layer=1):
     return out, ref, pool, host, g, bt, q
 
 
-@pytest.mark.parametrize("D", [64, 128])
+# path 1 = mma.sync kernel, 2 = tcgen05/TMEM kernel (head_dim 128)
+PATHS = [(64, 1), (128, 1), (128, 2)]
+
+
+@pytest.mark.parametrize("D,path", PATHS)
 @pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 2), (8, 1)])
-def test_prefill_matches_oracle(vk, D, Hq, Hkv):
+def test_prefill_matches_oracle(vk, D, path, Hq, Hkv):
     rng = np.random.default_rng(D + Hq + 10 * Hkv)
-    out, ref, *_ = _run(vk, rng, D, Hq, Hkv, T=100, pos=[0, 7, 300])
-    assert_close_attn(out, ref, "prefill D%d Hq%d Hkv%d" % (D, Hq, Hkv))
+    out, ref, *_ = _run(vk, rng, D, Hq, Hkv, T=100, pos=[0, 7, 300], path=path)
+    assert_close_attn(out, ref, "prefill D%d path%d Hq%d Hkv%d" % (D, path, Hq, Hkv))
 
 
-@pytest.mark.parametrize("T", [1, 15, 64, 65, 200])
-def test_prefill_chunk_lengths(vk, T):
+@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("T", [1, 15, 64, 65, 127, 128, 129, 200, 300])
+def test_prefill_chunk_lengths(vk, T, path):
     rng = np.random.default_rng(300 + T)
-    out, ref, *_ = _run(vk, rng, 128, 4, 2, T=T, pos=[0, 33, 129])
-    assert_close_attn(out, ref, "prefill T=%d" % T)
+    out, ref, *_ = _run(vk, rng, 128, 4, 2, T=T, pos=[0, 33, 129], path=path)
+    assert_close_attn(out, ref, "prefill T=%d path%d" % (T, path))
 
 
-def test_prefill_poisoned_pool(vk):
+@pytest.mark.parametrize("path", [1, 2])
+def test_prefill_poisoned_pool(vk, path):
     """Slots outside prefix + chunk hold NaN; outputs stay finite and match."""
     rng = np.random.default_rng(31)
-    out, ref, *_ = _run(vk, rng, 128, 8, 2, T=70, pos=[3, 64, 90], poison=True)
-    assert_close_attn(out, ref, "prefill poisoned")
+    out, ref, *_ = _run(vk, rng, 128, 8, 2, T=70, pos=[3, 64, 90], poison=True, path=path)
+    assert_close_attn(out, ref, "prefill poisoned path%d" % path)
+
+
+def test_prefill_paths_agree(vk):
+    """tcgen05 and mma.sync kernels agree within the attention tolerance."""
+    rng = np.random.default_rng(34)
+    a, ref, pool, host, g, bt, q = _run(vk, rng, 128, 8, 8, T=333, pos=[0, 700, 1500], path=1)
+    pool.set_prefill_path(2)
+    b = pool.prefill(1, dev_f16(q), dev_i32(bt), dev_i32([0, 700, 1500])).float().cpu().numpy()
+    assert_close_attn(b, ref, "tcgen05 vs oracle")
+    assert_close_attn(b, a, "tcgen05 vs mma.sync")
 
 
 def test_prefill_last_row_equals_decode(vk):

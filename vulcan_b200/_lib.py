@@ -62,6 +62,7 @@ SIGNATURES = {
     "vk_decode_run": (c_i32, [vp, vp, c_i32, vp, vp, vp, c_i32, vp, vp, c_f32, vp, vp]),
     "vk_set_decode_split": (c_i32, [vp, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
+    "vk_set_prefill_path": (c_i32, [vp, c_i32]),
     "vk_copy_pages": (c_i32, [vp, vp, vp, c_i32, vp]),
     "vk_remap_block_tables": (c_i32, [vp, c_i64, vp, c_i32, vp]),
     "vk_compact_plan": (c_i32, [vp, i32p, i32p, c_i32, i32p]),

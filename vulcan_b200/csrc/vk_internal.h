@@ -47,8 +47,10 @@ struct vk_pool {
     uint64_t head_bytes = 0;   // K block + V block of one (page, layer, head)
     int32_t num_pages = 0;
     uint32_t* d_err = nullptr;  // device error word (VK_ERR_* bits)
-    alignas(64) CUtensorMap tmap;  // 2-D view: rows of head_dim fp16 over the whole pool
+    alignas(64) CUtensorMap tmap;    // 2-D view: rows of head_dim fp16, boxes of 64 x 32 rows (K+V)
+    alignas(64) CUtensorMap tmap16;  // same view, boxes of 64 x 16 rows (K or V of one page)
     bool tmap_ok = false;
+    int32_t prefill_path = 0;        // 0 auto, 1 mma.sync kernel, 2 tcgen05 kernel
     int32_t split_override = 0;
     int32_t num_sms = vk::kNumSmsDefault;
     vk::Allocator alloc;
@@ -82,5 +84,7 @@ vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* ds
 vk_status launch_remap(int32_t* bt, int64_t entries, const int32_t* map, int map_len,
                        cudaStream_t st);
 int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len);
+vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const int32_t* bt, int bt_stride,
+                     const int32_t* positions, int B, int T, int Hq, float scale, cudaStream_t st);
 
 }  // namespace vk

@@ -105,10 +105,15 @@ static vk_status make_tmap(vk_pool* p) {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(p->cfg.head_dim), rows};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(p->cfg.head_dim) * 2};
     cuuint32_t box[2] = {64, static_cast<cuuint32_t>(2 * p->cfg.page_tokens)};
+    cuuint32_t box16[2] = {64, static_cast<cuuint32_t>(p->cfg.page_tokens)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(&p->tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p->base, dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+        r = encode(&p->tmap16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p->base, dims, strides, box16, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         char buf[96];
         std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);

@@ -307,5 +307,16 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
     p.scale_log2 = sc * 1.4426950408889634f;
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
+    const bool tc = D == 128 && pool->prefill_path != 1;
+    if (pool->prefill_path == 2 && !tc) return fail(VK_UNSUPPORTED, "the tcgen05 prefill supports head_dim 128");
+    if (tc)
+        return prefill_tc(pool, layer, q, out, block_tables, bt_stride, positions, batch, tokens, num_q_heads, scale,
+                          st);
     return D == 128 ? launch_prefill_t<128>(pool, p, batch, st) : launch_prefill_t<64>(pool, p, batch, st);
+}
+
+extern "C" vk_status vk_set_prefill_path(vk_pool* pool, int32_t path) {
+    if (!pool || path < 0 || path > 2) return fail(VK_INVALID_ARG, "path must be 0 (auto), 1 (mma.sync) or 2 (tcgen05)");
+    pool->prefill_path = path;
+    return VK_OK;
 }

@@ -1,0 +1,430 @@
+// K3 chunked prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same contract and arithmetic as the mma.sync prefill in vk_prefill.cu (the
+// causal j <= row rule of cpu_attention, tests/test_attention.cu:66-97, over a
+// cached prefix), head_dim 128.  One CTA per (128-query tile, query head,
+// sequence), one CTA per SM:
+//
+//  * warp 5 allocates 512 TMEM columns (S ping-pong buffers at columns 0 and
+//    128, the O accumulator at 256) and one thread issues every tcgen05.mma:
+//    S_j = Q K_j^T (M=128 queries, N=128 keys, K=128) into S[j%2], then after
+//    softmax_j: O += P_j V_j (M=128, N=128 head dims, K=128 keys).  Completions
+//    are tcgen05.commit arrivals on mbarriers.  Order on the tensor pipe:
+//    S_0, S_1, PV_0, S_2, PV_1, S_3, ... so S_{j+1} runs during softmax_j.
+//  * warp 4 lane 0 streams K and V pages with 2-D TMA boxes of 16 rows x 128 B
+//    (128-byte swizzle) into separate 2-stage K and V rings; a K stage is freed
+//    when its S MMA completes, a V stage when its PV MMA completes.
+//  * warps 0-3: one thread per query row (its TMEM lane).  tcgen05.ld of the S
+//    row, causal mask, row max, P = 2^(s - m) in fp16 written to shared memory in
+//    the UMMA K-major swizzled layout; O is rescaled in TMEM only when the row
+//    max grows by more than 8 (P stays <= 2^8, exact after the final divide).
+//  * All waits are bounded; V rows of keys at or beyond the written length are
+//    zeroed in shared memory before the last PV so stale bytes cannot reach O.
+#include "vk_internal.h"
+#include "vk_ptx.cuh"
+
+namespace vk {
+
+constexpr int kTcRows = 128;
+constexpr int kTcKeys = 128;
+constexpr int kTcThreads = 192;
+constexpr int kTcD = 128;
+// shared memory map (bytes from a 1024-aligned base)
+constexpr int kTcQ = 0;                       // [2 halves][128 rows][128 B]
+constexpr int kTcK = 32768;                   // 2 stages x 32 KiB
+constexpr int kTcV = kTcK + 2 * 32768;        // 2 stages x 32 KiB
+constexpr int kTcP = kTcV + 2 * 32768;        // [2 halves][128 rows][128 B]
+constexpr int kTcBar = kTcP + 32768;          // mbarriers + TMEM address
+constexpr int kTcSmem = kTcBar + 256 + 1024;
+constexpr uint32_t kTcCols = 512;
+
+struct TcParams {
+    const __half* q;
+    __half* out;
+    const int32_t* bt;
+    const int32_t* pos;
+    uint32_t* err;
+    int bt_stride, T, Hq, Hkv, G, layer, num_pages, q_tiles;
+    float scale_log2;
+};
+
+// ---------------------------------------------------------------- tcgen05 PTX
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory descriptor, 128-byte swizzle: start address, leading and
+// stride byte offsets (16-byte units), layout version 1, swizzle mode 2.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return static_cast<uint64_t>((smem_addr & 0x3FFFF) >> 4) | (static_cast<uint64_t>(lbo_bytes >> 4) << 16) |
+           (static_cast<uint64_t>(sbo_bytes >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, fp16 A and B, A K-major,
+// B K-major (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = 128.
+__device__ __forceinline__ constexpr uint32_t idesc_f16_128x128(uint32_t b_mn) {
+    return (1u << 4) | (b_mn << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, uint32_t* err) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap16,
+                                                                  const TcParams p) {
+    constexpr int P = kPageTokens;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBar);
+    // barrier slots
+    uint64_t* k_full = bars + 0;   // [2]
+    uint64_t* k_empty = bars + 2;  // [2]
+    uint64_t* v_full = bars + 4;   // [2]
+    uint64_t* v_empty = bars + 6;  // [2]
+    uint64_t* s_full = bars + 8;   // [2]
+    uint64_t* p_full = bars + 10;  // softmax -> MMA (count 128)
+    uint64_t* o_full = bars + 11;  // PV done
+    uint64_t* q_full = bars + 12;  // Q in shared memory (count 128)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos0 = p.pos[b];
+    const int q0 = qt * kTcRows;
+    if (pos0 < 0 || (pos0 + p.T + P - 1) / P > p.bt_stride) {
+        if (threadIdx.x == 0 && qt == 0 && h == 0) atomicOr(p.err, VK_ERR_TABLE_INDEX);
+        return;
+    }
+    const int kv_len = pos0 + min(p.T, q0 + kTcRows);
+    const int ntiles = (kv_len + kTcKeys - 1) / kTcKeys;
+    const int hkv = h / p.G;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_init(smem_u32(&s_full[0]), 1);
+        mbar_init(smem_u32(&s_full[1]), 1);
+        mbar_init(smem_u32(p_full), 128);
+        mbar_init(smem_u32(o_full), 1);
+        mbar_init(smem_u32(q_full), 128);
+        mbar_fence_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(smem_u32(tmem_slot), kTcCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tmap(&tmap16);
+            const uint64_t pol = l2_evict_first_policy();
+            const int32_t* btrow = p.bt + static_cast<int64_t>(b) * p.bt_stride;
+            bool ok = true;
+            for (int j = 0; j < ntiles && ok; ++j) {
+                const int st = j & 1;
+                const int npg = min(kTcKeys / P, (kv_len - j * kTcKeys + P - 1) / P);
+                int pages[kTcKeys / P];
+                for (int i = 0; i < npg; ++i) {
+                    int pg = btrow[j * (kTcKeys / P) + i];
+                    if (pg < 0 || pg >= p.num_pages) {
+                        atomicOr(p.err, VK_ERR_PAGE_ID);
+                        pg = 0;
+                    }
+                    pages[i] = pg;
+                }
+                for (int kv = 0; kv < 2 && ok; ++kv) {  // K ring, then V ring
+                    uint64_t* full = kv ? v_full : k_full;
+                    uint64_t* empty = kv ? v_empty : k_empty;
+                    if (j >= 2 && !mbar_wait(smem_u32(&empty[st]), ((j >> 1) - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&full[st]);
+                    mbar_expect_tx(bar, npg * 2 * (P * 128));
+                    const uint32_t dst0 = sbase + (kv ? kTcV : kTcK) + st * 32768;
+                    for (int i = 0; i < npg; ++i) {
+                        const int row = ((p.layer * p.num_pages + pages[i]) * p.Hkv + hkv) * (2 * P) + kv * P;
+#pragma unroll
+                        for (int hb = 0; hb < 2; ++hb)
+                            tma_load_2d(dst0 + hb * 16384 + i * (P * 128), &tmap16, hb * 64, row, bar, pol);
+                    }
+                }
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16_128x128(0), id_pv = idesc_f16_128x128(1);
+            bool ok = mbar_wait(smem_u32(q_full), 0, p.err);
+            tc_fence_after();
+            auto issue_s = [&](int j) {
+                const int st = j & 1;
+                ok = ok && mbar_wait(smem_u32(&k_full[st]), (j >> 1) & 1, p.err);
+                if (!ok) return;
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kTcD / 16; ++ks) {
+                    const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+                    umma_f16(tmem + st * 128, umma_desc_sw128(sbase + kTcQ + off, 16, 1024),
+                             umma_desc_sw128(sbase + kTcK + st * 32768 + off, 16, 1024), id_s, ks > 0);
+                }
+                umma_commit(smem_u32(&s_full[st]));
+                umma_commit(smem_u32(&k_empty[st]));
+            };
+            if (ok) issue_s(0);
+            if (ok && ntiles > 1) issue_s(1);
+            for (int j = 0; j < ntiles && ok; ++j) {
+                const int st = j & 1;
+                ok = mbar_wait(smem_u32(p_full), j & 1, p.err) && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kTcKeys / 16; ++ks) {
+                    const uint64_t a = umma_desc_sw128(sbase + kTcP + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+                    const uint64_t bv = umma_desc_sw128(sbase + kTcV + st * 32768 + ks * 2048, 16384, 1024);
+                    umma_f16(tmem + 256, a, bv, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(o_full));
+                umma_commit(smem_u32(&v_empty[st]));
+                if (j + 2 < ntiles) issue_s(j + 2);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax (one query row per thread)
+        const int r = threadIdx.x;  // 0..127 = TMEM lane
+        const int qrow = q0 + r;
+        const bool valid_row = qrow < p.T;
+        const int qpos = pos0 + qrow;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        // Q row -> shared memory (K-major, 128-byte swizzle)
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(
+                p.q + ((static_cast<int64_t>(b) * p.T + (valid_row ? qrow : 0)) * p.Hq + h) * kTcD);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                uint4 v = valid_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                const uint32_t addr = sbase + kTcQ + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                             "r"(v.w)
+                             : "memory");
+            }
+            fence_async_smem();
+            mbar_arrive(smem_u32(q_full));
+        }
+        float m_ref = -INFINITY, l = 0.f;
+        bool alive = true;
+        for (int j = 0; j < ntiles && alive; ++j) {
+            const int st = j & 1;
+            if (!wait_warp(smem_u32(&s_full[st]), (j >> 1) & 1, p.err)) { alive = false; break; }
+            tc_fence_after();
+            float s[kTcKeys];
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 32; ++c) {
+                float v[32];
+                tmem_ld32(lane_base + st * 128 + c * 32, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+            }
+            tmem_wait_ld();
+            const int key0 = j * kTcKeys;
+            const bool need_mask = key0 + kTcKeys - 1 > pos0 + q0;  // any key past the tile's first row
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kTcKeys; ++c) {
+                float v = s[c] * p.scale_log2;
+                if (need_mask && key0 + c > qpos) v = -INFINITY;
+                s[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            float alpha = 1.f;
+            if (mx > m_ref + 8.f || m_ref == -INFINITY) {  // lazy rescale
+                const float m_new = fmaxf(m_ref, mx);
+                alpha = ex2(m_ref - m_new);
+                m_ref = m_new;
+            }
+            float rowsum = 0.f;
+            uint32_t pk[kTcKeys / 2];
+#pragma unroll
+            for (int c = 0; c < kTcKeys; c += 2) {
+                const float a0 = ex2(s[c] - m_ref), a1 = ex2(s[c + 1] - m_ref);
+                rowsum += a0 + a1;
+                pk[c >> 1] = pack_half2(a0, a1);
+            }
+            l = l * alpha + rowsum;
+            // PV_{j-1} must be done before P is overwritten and O rescaled
+            if (j > 0) {
+                if (!wait_warp(smem_u32(o_full), (j - 1) & 1, p.err)) { alive = false; break; }
+                tc_fence_after();
+            }
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
+                const uint32_t addr = sbase + kTcP + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]),
+                             "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                             : "memory");
+            }
+            // tcgen05.ld/st are warp-collective: rescale if any row of the warp needs it
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < kTcD / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(lane_base + 256 + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= alpha;
+                    tmem_st32(lane_base + 256 + c * 32, v);
+                }
+                tmem_wait_st();
+            }
+            if (j == ntiles - 1 && key0 + kTcKeys > kv_len) {
+                // zero V rows of keys at or beyond the written length (last tile only)
+                if (!wait_warp(smem_u32(&v_full[st]), (j >> 1) & 1, p.err)) { alive = false; break; }
+                if (key0 + r >= kv_len) {
+#pragma unroll
+                    for (int hb = 0; hb < 2; ++hb)
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            const uint32_t addr = sbase + kTcV + st * 32768 + hb * 16384 + r * 128 + (c << 4);
+                            asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+                        }
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(smem_u32(p_full));
+        }
+        if (alive && wait_warp(smem_u32(o_full), (ntiles - 1) & 1, p.err)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            __half* dst = p.out + ((static_cast<int64_t>(b) * p.T + (valid_row ? qrow : 0)) * p.Hq + h) * kTcD;
+#pragma unroll
+            for (int c = 0; c < kTcD / 32; ++c) {
+                float v[32];
+                tmem_ld32(lane_base + 256 + c * 32, v);
+                tmem_wait_ld();
+                if (valid_row) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 w;
+                        w.x = pack_half2(v[i] * inv, v[i + 1] * inv);
+                        w.y = pack_half2(v[i + 2] * inv, v[i + 3] * inv);
+                        w.z = pack_half2(v[i + 4] * inv, v[i + 5] * inv);
+                        w.w = pack_half2(v[i + 6] * inv, v[i + 7] * inv);
+                        *reinterpret_cast<uint4*>(dst + c * 32 + i) = w;
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTcCols);
+    }
+}
+
+vk_status launch_prefill_tc(vk_pool* pool, const TcParams& p, int B, cudaStream_t st) {
+    static uint64_t attr_set = 0;
+    const uint64_t bit = 1ull << (pool->device & 63);
+    if (!(attr_set & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
+        attr_set |= bit;
+    }
+    dim3 grid(p.q_tiles, p.Hq, B);
+    prefill_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(pool->tmap16, p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "prefill_tc_kernel launch");
+}
+
+vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const int32_t* bt, int bt_stride,
+                     const int32_t* positions, int B, int T, int Hq, float scale, cudaStream_t st) {
+    TcParams p;
+    p.q = static_cast<const __half*>(q);
+    p.out = static_cast<__half*>(out);
+    p.bt = bt;
+    p.pos = positions;
+    p.err = pool->d_err;
+    p.bt_stride = bt_stride;
+    p.T = T;
+    p.Hq = Hq;
+    p.Hkv = pool->cfg.num_kv_heads;
+    p.G = Hq / p.Hkv;
+    p.layer = layer;
+    p.num_pages = pool->num_pages;
+    p.q_tiles = (T + kTcRows - 1) / kTcRows;
+    const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(kTcD));
+    p.scale_log2 = sc * 1.4426950408889634f;
+    return launch_prefill_tc(pool, p, B, st);
+}
+
+}  // namespace vk

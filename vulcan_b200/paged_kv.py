@@ -214,6 +214,10 @@ class PagedKVPool:
                                    _stream(stream)), "vk_prefill")
         return out
 
+    def set_prefill_path(self, path: int) -> None:
+        """0 automatic, 1 mma.sync kernel, 2 tcgen05/TMEM kernel."""
+        check(self._lib.vk_set_prefill_path(self.handle, path), "vk_set_prefill_path")
+
     def copy_pages(self, src_ids: torch.Tensor, dst_ids: torch.Tensor, stream=None) -> None:
         _need(src_ids, torch.int32, "src_ids")
         _need(dst_ids, torch.int32, "dst_ids")
