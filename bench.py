@@ -249,6 +249,10 @@ def main():
     ap.add_argument("--eager", action="store_true", help="launch every layer from Python instead of a CUDA graph")
     ap.add_argument("--no-early-start", action="store_true",
                     help="launch each layer's decode only after the previous one completes")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "p2p-wait", "nccl"],
+                    help="head-sharded output allgather: peer stores fused into the decode, overlapping the "
+                         "next layer (p2p) or waited for before the next layer reads its inputs (p2p-wait); "
+                         "or NCCL on a side stream")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
     ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
     args = ap.parse_args()
@@ -328,12 +332,19 @@ def main():
     plan_ws = torch.empty(pool.plan(lens_host, hq_l).workspace.numel() + 4096, dtype=torch.uint8, device=dev)
     gathered = None
     comm = None
+    gat = None
     if world > 1 and wl["shard"] == "head":
-        gathered = torch.empty(L, world, Bl, hq_l, D, device=dev, dtype=torch.float16)
-        comm = torch.cuda.Stream(device=dev)
+        if args.gather.startswith("p2p") and args.path == "planned":
+            # receive buffers of every layer on every rank, written by the decode;
+            # 2L slots so that alternate steps of the e2e run use alternate halves
+            gat = vk.Gather(rank, world, Bl * hq_l * D * 2, slots=2 * L, device=dev)
+            gat.exchange()
+        else:
+            gathered = torch.empty(L, world, Bl, hq_l, D, device=dev, dtype=torch.float16)
+            comm = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
     merge_launched = 1 if pool.workspace_size(Bl, hq_l, max_len) > 0 else 0
-    launches_per_step = L * (2 + merge_launched) if args.path == "split" else L
+    launches_per_step = (L * (2 + merge_launched) if args.path == "split" else L) + (1 if gat is not None else 0)
 
     use_graph = not args.eager
     plan_keep = {}
@@ -344,6 +355,8 @@ def main():
             p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
             if not args.no_early_start:
                 p_.set_early_start(True)  # layers are back to back: overlap each launch's start
+            if gat is not None:
+                p_.set_gather(gat, slot_base=0, wait_prev=args.gather == "p2p-wait")
             p_.upload()
             plan_keep["plan"] = p_
 
@@ -358,7 +371,7 @@ def main():
             if args.path == "split":
                 pool.decode(l, q[l], bt_d, lens_d, max_len, out=out[l], workspace=ws)
             else:
-                plan.run(l, q[l], bt_d, out=out[l], k_new=kn3[l], v_new=vn3[l])
+                plan.run(l, q[l], bt_d, out=None if gat is not None else out[l], k_new=kn3[l], v_new=vn3[l])
             if events is not None:
                 events[l][1].record(cur)
             if gathered is not None:
@@ -369,6 +382,8 @@ def main():
                     dist.all_gather_into_tensor(gathered[l].view(-1), out[l].view(-1))
         if gathered is not None:
             cur.wait_stream(comm)
+        if gat is not None:
+            gat.wait(L - 1)  # the last layer's slices from every rank
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -380,6 +395,8 @@ def main():
         new_plan()
         layers()
     pool.check()  # no device errors during warm-up
+    if gat is not None:
+        gat.check()
     barrier()
 
     graph = None
@@ -450,7 +467,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world,
-                      gathered, comm, lens_host, plan_ws, use_graph)
+                      gathered, comm, lens_host, plan_ws, use_graph, gat)
         e2e["value"] = B / (e2e.pop("ms_step") * 1e-3)
 
     # --- CPU baseline (rank 0 at N=1 only): oracle port, 1 thread, bounded sample
@@ -473,8 +490,14 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded N(0,0.5^2) fp16 K/V/Q, random block tables)",
             "config": {"workload": wl["desc"], "shard": wl["shard"] if world > 1 else "none",
-                       "parallelism": ("kv-head shard x%d + NCCL allgather" % world if wl["shard"] == "head"
-                                       else "sequence shard x%d" % world) if world > 1 else "single GPU",
+                       "parallelism": ("kv-head shard x%d + %s" % (world, "allgather fused into the decode "
+                                                                      "(peer stores over NVLink, flag per layer)"
+                                                                      + (", each layer waits for the previous "
+                                                                         "layer's gather" if args.gather == "p2p-wait"
+                                                                         else "")
+                                                                      if gat is not None else "NCCL allgather")
+                                       if wl["shard"] == "head" else "sequence shard x%d" % world)
+                                      if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: %.1f GB of K/V read per step" % (ab_job["decode"] * L / 1e9),
                        "decode_path": args.path,
                        "launch": "CUDA graph of the %d-layer step" % L if use_graph else "eager",
@@ -495,7 +518,12 @@ def main():
             "e2e": e2e,
         }
         print(json.dumps(line), flush=True)
+    pool.check()
+    if gat is not None:
+        gat.check()
     del graph
+    if gat is not None:
+        gat.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -743,7 +771,7 @@ def run_prefill(args, wl):
 
 
 def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world, gathered, comm,
-            lens_host, plan_ws, use_graph):
+            lens_host, plan_ws, use_graph, gat=None):
     """Same step through the public API with host buffers: each layer's q/k/v is
     copied from pinned host memory to the device on a copy stream (double
     buffered, overlapping the previous layer's kernel) and each layer's output
@@ -756,7 +784,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     hq = (torch.randn(L, Bl, hq_l, D, generator=g) * 0.5).half().pin_memory()
     hk = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
     hv = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
-    gathered_host = gathered is not None
+    gathered_host = gathered is not None or gat is not None
     out_shape = (L, world, Bl, hq_l, D) if gathered_host else (L, Bl, hq_l, D)
     hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
     nbuf = 2
@@ -771,13 +799,18 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     d2h_bytes = hout.numel() * 2
     plan_keep = {}
 
-    def new_plan():
+    def new_plan(parity=0):
         if args.path == "planned":
             p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+            if gat is not None:
+                # alternate steps write alternate halves of the 2L slots, so a
+                # slot is rewritten only after every rank's copies of it are done
+                p_.set_gather(gat, slot_base=parity * L, wait_prev=args.gather == "p2p-wait")
             p_.upload()
             plan_keep["plan"] = p_
 
-    def layers():
+    def layers(parity=0):
+        base = parity * L
         cur = torch.cuda.current_stream(dev)
         plan = plan_keep.get("plan")
         h2d.wait_stream(cur)
@@ -810,11 +843,19 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
                 pool.append(l, dk[s].view(Bl, 1, hkv_l, D), dv[s].view(Bl, 1, hkv_l, D), bt_d, pos_d)
                 pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
             else:
-                plan.run(l, dq[s], bt_d, out=douts[s], k_new=dk[s], v_new=dv[s])
+                plan.run(l, dq[s], bt_d, out=None if gat is not None else douts[s], k_new=dk[s], v_new=dv[s])
             fe = torch.cuda.Event()
             fe.record(cur)
             freed[s] = fe
-            if gathered_host:
+            if gat is not None:
+                # slot l-1 is complete once run l (which waited for it) is done
+                # the copy stream waits for every rank's slice of this layer
+                # (a bounded flag wait on peers' stores), then reads the slot
+                d2h.wait_event(fe)
+                with torch.cuda.stream(d2h):
+                    gat.wait(base + l, stream=d2h)
+                    hout[l].copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
+            elif gathered_host:
                 comm.wait_event(fe)
                 with torch.cuda.stream(comm):
                     dist.all_gather_into_tensor(gathered[l].view(-1), douts[s].view(-1))
@@ -825,11 +866,12 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             else:
                 d2h.wait_event(fe)
                 src = douts[s]
-            with torch.cuda.stream(d2h):
-                hout[l].copy_(src, non_blocking=True)
-                od = torch.cuda.Event()
-                od.record(d2h)
-                outdone[s] = od
+            if gat is None:
+                with torch.cuda.stream(d2h):
+                    hout[l].copy_(src, non_blocking=True)
+                    od = torch.cuda.Event()
+                    od.record(d2h)
+                    outdone[s] = od
         cur.wait_stream(d2h)
         cur.wait_stream(h2d)
 
@@ -839,27 +881,38 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    counter = [0]
     for _ in range(args.warmup):
-        new_plan()
-        layers()
+        par = counter[0] % 2
+        counter[0] += 1
+        new_plan(par)
+        layers(par)
     barrier()
     graph = None
+    graphs = []
     per_layer_events = True
     if use_graph:
-        graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(device=dev)
-        cap.wait_stream(compute)
-        with torch.cuda.graph(graph, stream=cap):
-            layers()
-        compute.wait_stream(cap)
+        for par in ((0, 1) if gat is not None else (0,)):
+            g_ = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(device=dev)
+            cap.wait_stream(compute)
+            new_plan(par)
+            with torch.cuda.graph(g_, stream=cap):
+                layers(par)
+            compute.wait_stream(cap)
+            graphs.append(g_)
 
         def step():
-            new_plan()
-            graph.replay()
+            par = counter[0] % len(graphs)
+            counter[0] += 1
+            new_plan(par)
+            graphs[par].replay()
     else:
         def step():
-            new_plan()
-            layers()
+            par = counter[0] % 2
+            counter[0] += 1
+            new_plan(par)
+            layers(par)
     step()
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -874,7 +927,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    del graph
+    del graph, graphs
     return {"ms_step": ms / args.steps, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h_bytes),
             "path": "PagedKVPool / DecodePlan (C ABI) with pinned host q, k, v and outputs; H2D and D2H on "

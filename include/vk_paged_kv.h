@@ -198,6 +198,10 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace,
  * step).  Default off. */
 vk_status vk_decode_plan_set_early_start(vk_decode_plan* plan, int32_t enable);
 
+/* Caps the workers of plans made after the call (0 = one per resident warp,
+ * the default); a tuning aid for small per-GPU shares. */
+vk_status vk_set_decode_workers(vk_pool* pool, int32_t max_workers);
+
 /* Plan facts: 0 workers, 1 CTAs, 2 partial slots, 3 total pages, 4 longest
  * sequence in pages; -1 for an unknown query. */
 int32_t   vk_decode_plan_info(const vk_decode_plan* plan, int32_t what);
@@ -205,6 +209,62 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
                         void* out, const int32_t* block_tables, int32_t bt_stride,
                         const void* k_new, const void* v_new, float scale, void* workspace,
                         void* stream);
+
+/* ---- Head-sharded output all-gather fused into the planned decode ---------
+ * KV-head sharding over `world` GPUs of one node (one process per GPU): rank r
+ * owns a contiguous block of KV heads and their query heads, and every rank
+ * needs the whole [B, Hq, D] output of each layer.  Instead of a separate
+ * collective, the planned decode bound to a gather writes each finished
+ * (sequence, KV head) output straight into every rank's receive buffer with
+ * peer stores over NVLink, and when its last unit of the layer is out it raises
+ * this rank's flag in every rank's flag block.  No multicast is used.
+ *
+ * Receive buffer of each rank: `slots` slots of [world][slice_bytes]; rank r's
+ * slice of a slot holds its [B, Hq/world, D] fp16 output of one layer (the
+ * layout ncclAllGather gives).  Setup (host):
+ *   vk_gather_create(device, rank, world, slice_bytes, slots, &g)
+ *   vk_gather_export(g, handle)            VK_GATHER_HANDLE_BYTES opaque bytes
+ *   ... exchange handles between the ranks (any host transport) ...
+ *   vk_gather_import(g, peer, peer_handle) for every peer != rank
+ *   vk_decode_plan_set_gather(plan, g, slot_base, wait_prev)
+ * A run of layer l writes slot (slot_base + l) % slots.  With a gather bound,
+ * vk_decode_run's `out` may be NULL (the rank's own slice of the slot is
+ * written), else it must be 16-byte aligned and is written as well.  With
+ * wait_prev = 1, every run first waits (bounded, 1 s; VK_ERR_TIMEOUT on
+ * expiry) until all ranks' slices of the slot before its own have arrived,
+ * before it reads q, k_new or v_new: the order of a model whose next layer
+ * consumes the gathered output.  With wait_prev = 0 the gather of layer l
+ * overlaps layer l+1 (the order of an all-gather on a side stream), and
+ * vk_gather_wait makes a stream wait for one slot; since each rank raises its
+ * flags in layer order, waiting for the slot of a step's last layer covers the
+ * step.  The library does not order a slot's reuse against the readers of a
+ * receive buffer: callers rewrite a slot only after a wait that follows its
+ * readers on every rank (for example slot_base 0 and L on alternate steps of
+ * L layers, with 2L slots).  No reference counterpart: the reference runs on
+ * one GPU. */
+#define VK_GATHER_HANDLE_BYTES 64
+typedef struct vk_gather vk_gather;
+
+vk_status vk_gather_create(int32_t device, int32_t rank, int32_t world, uint64_t slice_bytes,
+                           int32_t slots, vk_gather** out_gather);
+/* Teardown in two phases: every rank calls vk_gather_release_peers (waits
+ * for the device, closes its mappings of the peers' buffers), the ranks meet
+ * at a host barrier, then each calls vk_gather_destroy (frees its own buffer,
+ * which no peer maps any more).  vk_gather_destroy alone releases first. */
+vk_status vk_gather_release_peers(vk_gather* g);
+vk_status vk_gather_destroy(vk_gather* g);
+vk_status vk_gather_export(const vk_gather* g, void* handle_out);
+vk_status vk_gather_import(vk_gather* g, int32_t peer, const void* handle);
+/* This rank's receive buffer of one slot: [world][slice_bytes] (NULL if bad). */
+void*     vk_gather_buffer(const vk_gather* g, int32_t slot);
+vk_status vk_gather_wait(vk_gather* g, int32_t slot, void* stream);
+/* Synchronous: VK_TIMEOUT if a vk_gather_wait gave up since the last check
+ * (timeouts inside vk_decode_run are reported by vk_pool_check). */
+vk_status vk_gather_check(vk_gather* g);
+/* Binds (g != NULL) or unbinds (g == NULL) a gather; slice_bytes must cover
+ * the plan's [B, Hq, D] fp16 output, and every peer must be imported. */
+vk_status vk_decode_plan_set_gather(vk_decode_plan* plan, vk_gather* g, int32_t slot_base,
+                                    int32_t wait_prev);
 
 /* ---- K3: chunked prefill -------------------------------------------------
  * The prefill use of launch_attention (src/transformer.cpp:136-189 with

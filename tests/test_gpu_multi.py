@@ -1,9 +1,11 @@
-"""Two-GPU test of KV-head-sharded decode with the NCCL all-gather: each rank
-holds half of the KV heads of a 70B-shaped pool, decodes its query heads with
-the planned kernel (fused append), and the all-gathered output matches a
-single-GPU decode of the full pool within the attention tolerance.  Skipped
-when fewer than two GPUs are visible.  Child processes, NVLS off, short
-process-group timeout."""
+"""Two-GPU tests of KV-head-sharded decode: each rank holds half of the KV
+heads of a 70B-shaped pool and decodes its query heads with the planned kernel
+(fused append).  The output all-gathered by NCCL, and the output gathered by
+the decode's own peer stores (vk_gather, two layers back to back with the
+previous-slot wait), both match a single-GPU decode of the full pool within the
+attention tolerance, and the two gathers agree bit for bit.  Skipped when fewer
+than two GPUs are visible.  Child processes, NVLS off, short process-group
+timeout."""
 import datetime
 import os
 import socket
@@ -65,8 +67,28 @@ def _worker(rank, world, port, results):
         gathered = torch.empty(world, *out.shape, dtype=out.dtype, device=dev)
         dist.all_gather_into_tensor(gathered.view(-1), out.contiguous().view(-1))
         full = gathered_to_heads(gathered).float().cpu()
+        # the same layer through the fused peer-store gather: layer 0 then
+        # layer 1 (which waits for layer 0's slot), append only in layer 1 of
+        # a fresh copy of the shard
+        lp2 = vk.PagedKVPool(g.L, sh.num_kv_heads, g.D, g.num_pages)
+        lp2.kv_view().copy_(torch.from_numpy(np.ascontiguousarray(pool[:, :, sh.kv_lo:sh.kv_hi])).view(torch.float16))
+        B = len(lens)
+        gat = vk.Gather(rank, world, B * sh.num_q_heads * g.D * 2, slots=2)
+        gat.exchange()
+        gplan = lp2.plan(lens.tolist(), sh.num_q_heads)
+        gplan.set_gather(gat, wait_prev=True)
+        qd = torch.from_numpy(np.ascontiguousarray(q[:, sh.q_lo:sh.q_hi])).to(dev)
+        gplan.run(0, qd, bt_d)
+        gplan.run(1, qd, bt_d, k_new=torch.from_numpy(np.ascontiguousarray(kn[:, sh.kv_lo:sh.kv_hi])).to(dev),
+                  v_new=torch.from_numpy(np.ascontiguousarray(vn[:, sh.kv_lo:sh.kv_hi])).to(dev))
+        gat.wait(1)
+        fused = gat.view(1, B, sh.num_q_heads, g.D)
+        torch.cuda.synchronize()
+        gat.check()
+        lp2.check()
+        same = bool(torch.equal(fused, gathered))
         lp.check()
-        ok = True
+        ok = same
         if rank == 0:  # single-GPU reference on the whole pool
             fp = vk.PagedKVPool(g.L, g.Hkv, g.D, g.num_pages)
             fp.kv_view().copy_(torch.from_numpy(pool).view(torch.float16))
@@ -74,7 +96,9 @@ def _worker(rank, world, port, results):
                                                  k_new=torch.from_numpy(kn).to(dev),
                                                  v_new=torch.from_numpy(vn).to(dev)).float().cpu()
             err = (full - ref).abs()
-            ok = bool((err <= 2e-3 + 1e-2 * ref.abs()).all())
+            ok = same and bool((err <= 2e-3 + 1e-2 * ref.abs()).all())
+        gplan.set_gather(None)
+        gat.close()  # releases the peer mappings, barrier, frees
         results[rank] = ok
         dist.barrier()
         dist.destroy_process_group()

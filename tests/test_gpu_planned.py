@@ -121,3 +121,37 @@ def test_planned_rejects_narrow_table(vk):
     q = torch.zeros(1, 8, 128, dtype=torch.float16, device="cuda")
     with pytest.raises(vk.VKError):
         plan.run(0, q, torch.zeros(1, 3, dtype=torch.int32, device="cuda"))  # 100 tokens need 7 pages
+
+
+def test_planned_fused_gather_one_rank(vk):
+    """A gather of one rank: every layer's output lands in slot slot_base +
+    layer of the receive buffer, bit-identical to the plain run, with and
+    without an explicit `out`, with and without the previous-slot wait;
+    vk_gather_wait passes and no timeout is recorded."""
+    rng = np.random.default_rng(31)
+    lens = np.array([0, 1, 17, 300, 2049], np.int32)
+    Hq, Hkv, D, L = 16, 2, 128, 3
+    g, bt, host, q = _case(rng, lens, Hq, Hkv, D, L=L)
+    pool = make_pool(vk, g, host)
+    bt_d = dev_i32(bt)
+    plan = pool.plan(lens.tolist(), Hq)
+    plain = [plan.run(l, dev_f16(q), bt_d).clone() for l in range(L)]
+    B = len(lens)
+    gat = vk.Gather(0, 1, B * Hq * D * 2, slots=2 * L)
+    for step in range(4):
+        base = (step % 2) * L
+        gplan = pool.plan(lens.tolist(), Hq)
+        gplan.set_gather(gat, slot_base=base, wait_prev=step < 2)
+        for l in range(L):
+            explicit = torch.empty_like(plain[0]) if l == 1 else None
+            r = gplan.run(l, dev_f16(q), bt_d, out=explicit)
+            if explicit is not None:
+                assert torch.equal(r, plain[l])
+        gat.wait(base + L - 1)
+        for l in range(L):
+            assert torch.equal(gat.view(base + l, B, Hq, D)[0], plain[l]), "step %d layer %d" % (step, l)
+        gplan.set_gather(None)
+    torch.cuda.synchronize()
+    gat.check()
+    assert pool.check() == 0
+    gat.close()

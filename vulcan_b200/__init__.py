@@ -6,8 +6,8 @@ page copy and pinned-host swap.  This package binds it with ctypes and mirrors
 the reference's KVCache / MemoryManager / launch_attention interfaces.
 """
 from ._lib import VKError, load  # noqa: F401
-from .paged_kv import (DecodePlan, KVCache, MemoryManager, PagedKVPool, default_scale,  # noqa: F401
+from .paged_kv import (DecodePlan, Gather, KVCache, MemoryManager, PagedKVPool, default_scale,  # noqa: F401
                        launch_attention, remap_block_tables)
 
-__all__ = ["VKError", "load", "DecodePlan", "KVCache", "MemoryManager", "PagedKVPool", "default_scale",
+__all__ = ["VKError", "load", "DecodePlan", "Gather", "KVCache", "MemoryManager", "PagedKVPool", "default_scale",
            "launch_attention", "remap_block_tables"]

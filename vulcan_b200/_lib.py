@@ -61,6 +61,16 @@ SIGNATURES = {
     "vk_decode_plan_set_early_start": (c_i32, [vp, c_i32]),
     "vk_decode_run": (c_i32, [vp, vp, c_i32, vp, vp, vp, c_i32, vp, vp, c_f32, vp, vp]),
     "vk_set_decode_split": (c_i32, [vp, c_i32]),
+    "vk_set_decode_workers": (c_i32, [vp, c_i32]),
+    "vk_gather_create": (c_i32, [c_i32, c_i32, c_i32, c_u64, c_i32, ctypes.POINTER(vp)]),
+    "vk_gather_destroy": (c_i32, [vp]),
+    "vk_gather_release_peers": (c_i32, [vp]),
+    "vk_gather_export": (c_i32, [vp, vp]),
+    "vk_gather_import": (c_i32, [vp, c_i32, vp]),
+    "vk_gather_buffer": (vp, [vp, c_i32]),
+    "vk_gather_wait": (c_i32, [vp, c_i32, vp]),
+    "vk_gather_check": (c_i32, [vp]),
+    "vk_decode_plan_set_gather": (c_i32, [vp, vp, c_i32, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
     "vk_set_prefill_path": (c_i32, [vp, c_i32]),
     "vk_copy_pages": (c_i32, [vp, vp, vp, c_i32, vp]),

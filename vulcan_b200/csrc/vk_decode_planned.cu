@@ -14,17 +14,26 @@
 //  * Each worker warp prefetches its own pages NSTW ahead with 2-D TMA loads
 //    (one mbarrier per stage) and folds each page into its softmax state with
 //    the tensor-core page update shared with vk_decode.
-//  * Append fused: when a worker is about to load the last page of a unit and
-//    new K/V rows were given, the warp first writes the new token's rows into
-//    that page (fence.proxy.async orders them before the TMA read).
+//  * Append fused: the last page of a unit is loaded as it is; when new K/V
+//    rows were given, the consuming warp stores them into the pool and patches
+//    them into the staged copy before folding the page in, so no load waits for
+//    the new rows.
 //  * Merge fused: a unit covered by one worker writes its fp16 output directly;
-//    otherwise each piece writes its normalised partial and log2-sum-exp, and
-//    the last piece to finish (per-unit counter) merges them from L2 and resets
-//    the counter for the next launch.
+//    otherwise each piece writes its normalised partial and log2-sum-exp and
+//    counts itself on the unit.  Merges are tasks of (unit, group of query
+//    heads) dealt to all warps of the grid by the plan; a warp runs its tasks
+//    after its own page range, each once the unit's pieces are all counted
+//    (bounded wait).  No warp merges in the middle of its range, and the merge
+//    of a unit split into many pieces is spread over up to G warps.
+//  * Gather fused (optional, head-sharded multi-GPU): each finished unit output
+//    is also stored into every rank's receive slice over NVLink; the warp that
+//    counts the layer's last unit raises this rank's flag on every rank.  A run
+//    may first wait for all ranks' flags of the previous layer's slot.
 #include <algorithm>
 #include <vector>
 
 #include "vk_decode_page.cuh"
+#include "vk_gather.cuh"
 #include "vk_internal.h"
 
 namespace vk {
@@ -41,8 +50,9 @@ struct PlanParams {
     const int32_t* ufw;    // [U]   first worker touching the unit
     const int32_t* unp;    // [U]   workers touching the unit (pieces)
     const int32_t* uslot;  // [U]   first partial slot of the unit (-1 if one piece)
+    const int32_t* tunits; // [ntasks / S] unit of each merge task group
     const int32_t* zunits; // [Z]   units without pages (zero output)
-    uint32_t* counters;    // [U]   pieces finished (reset by the merging piece)
+    uint32_t* counters;    // [2U] pieces finished, merge tasks finished (reset by the last task)
     float* part_o;         // [slots, G, D]
     float* part_lse;       // [slots, G]
     const __half* q;
@@ -53,8 +63,15 @@ struct PlanParams {
     uint32_t* err;
     char* pool_base;
     uint64_t seg_bytes, layer_off, head_bytes;
-    int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z;
+    int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z, U;
+    int ntasks, S;   // merge tasks, tasks (head groups) per split unit
+    int ndone;       // units + extra tasks: completions that make a layer's output whole
     float scale_log2;
+    // fused output gather (g.world == 0: none)
+    GatherView g;
+    int gslot;       // slot this layer writes
+    int gwait_slot;  // slot to wait for before reading inputs (-1: none)
+    int out_own;     // out is this rank's own slice (skip the local copy)
 };
 
 template <int D>
@@ -72,15 +89,71 @@ __device__ __forceinline__ void griddep_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_global() {
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Writes zeros for a unit without pages (a sequence of length 0).
 template <int D>
 __device__ __forceinline__ void zero_unit(const PlanParams& p, int u, int lane) {
     __half* o = p.out + (static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G) * D;
     for (int e = lane; e < p.G * D; e += 32) o[e] = __float2half(0.f);
+}
+
+__device__ __forceinline__ void atom_add_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Fused gather: the warp that finished `nh` query heads of unit u starting at
+// head h (their [nh, D] outputs are in p.out) copies them in 16-byte pieces
+// into every rank's receive slice, then counts the completion; the warp
+// counting the layer's last completion raises this rank's flag.
+template <int D>
+__device__ __forceinline__ void publish_heads(const PlanParams& p, int u, int h, int nh, int lane) {
+    if (p.g.world == 0) return;
+    __syncwarp();
+    const int64_t head0 = static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G + h;
+    const uint4* src = reinterpret_cast<const uint4*>(p.out + head0 * D);
+    const uint64_t off = static_cast<uint64_t>(p.gslot) * p.g.slot_bytes +
+                         static_cast<uint64_t>(p.g.rank) * p.g.slice_bytes + static_cast<uint64_t>(head0) * D * 2;
+    const int n16 = nh * D / 8;
+    for (int c = lane; c < n16; c += 32) {
+        const uint4 v = __ldcg(src + c);  // written by other lanes of this warp
+        for (int r = 0; r < p.g.world; ++r) {
+            if (r == p.g.rank && p.out_own) continue;
+            reinterpret_cast<uint4*>(p.g.base[r] + off)[c] = v;
+        }
+    }
+    // __syncwarp orders every lane's peer stores before lane 0's release; the
+    // last completion acquires them all and releases them to the peers with
+    // the flag (one system-scope fence per layer instead of one per warp).
+    __syncwarp();
+    if (lane == 0) {
+        uint32_t* done = reinterpret_cast<uint32_t*>(p.g.base[p.g.rank] + p.g.done_off) + p.gslot;
+        if (atom_add_acq_rel_gpu(done, 1u) == static_cast<uint32_t>(p.ndone - 1)) {
+            *done = 0u;  // every completion of this layer is counted
+            gather_signal(p.g, p.gslot);
+        }
+    }
+    __syncwarp();
+}
+
+template <int D>
+__device__ __forceinline__ void publish_unit(const PlanParams& p, int u, int lane) {
+    publish_heads<D>(p, u, 0, p.G, lane);
+}
+
+// Fused gather: waits until the previous layer's slot is complete on this rank.
+__device__ __forceinline__ void wait_prev_slot(const PlanParams& p, int lane) {
+    if (p.gwait_slot < 0) return;
+    if (lane == 0) gather_wait_slot(p.g, p.gwait_slot, p.err);
+    __syncwarp();
 }
 
 // Iterator over (unit, page-in-unit) along the concatenated page list.
@@ -97,62 +170,147 @@ struct PageIt {
     }
 };
 
-// The last piece of a unit combines all pieces' partials (read from L2):
-// out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), streamed over k with a
-// running max.  Each lane owns float4 items f = lane + 32*i of the unit's
-// [G, D] output; all loads of one piece are issued together, so the merge costs
-// about one L2 round trip per piece.
+
+// One merge task: heads [h0, h0 + hs) of unit u from its np piece partials,
+// out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), written as fp16.  IT =
+// float4 items per lane (items f = lane + 32 i, i < IT, of the task's
+// [hs, D] block).  The lse pass reads up to 64 pieces per round (piece k in
+// lane k % 32); the o pass issues the loads of KB pieces together.
+template <int D, int NT, int IT>
+__device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, int hs, int np, int lane) {
+    constexpr int GMAX = 8 * NT;
+    constexpr int KMAX = 2;
+    constexpr int KB = 16 / IT;
+    const int base = p.uslot[u];
+    const int nf = hs * D / 4;
+    float m[GMAX], den[GMAX];
+#pragma unroll
+    for (int hh = 0; hh < GMAX; ++hh) {
+        m[hh] = -INFINITY;
+        den[hh] = 0.f;
+    }
+    for (int k0 = 0; k0 < np; k0 += 32 * KMAX) {
+        float lv[GMAX][KMAX];
+#pragma unroll
+        for (int hh = 0; hh < GMAX; ++hh)
+#pragma unroll
+            for (int r = 0; r < KMAX; ++r) {
+                const int k = k0 + r * 32 + lane;
+                lv[hh][r] = (hh < hs && k < np) ? __ldcg(p.part_lse + static_cast<int64_t>(base + k) * p.G + h0 + hh)
+                                                : -INFINITY;
+            }
+#pragma unroll
+        for (int hh = 0; hh < GMAX; ++hh) {
+            if (hh < hs) {
+                float mx = fmaxf(lv[hh][0], lv[hh][1]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float mn = fmaxf(m[hh], mx);
+                float e = 0.f;
+#pragma unroll
+                for (int r = 0; r < KMAX; ++r) e += ex2(lv[hh][r] - mn);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+                den[hh] = den[hh] * ex2(m[hh] - mn) + e;
+                m[hh] = mn;
+            }
+        }
+    }
+    float mi[IT], di[IT];
+    int hi[IT];
+    float4 acc[IT];
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+        const int f = lane + 32 * i;
+        hi[i] = f < nf ? (f * 4) / D : 0;
+        mi[i] = m[0];
+        di[i] = den[0];
+#pragma unroll
+        for (int q = 1; q < GMAX; ++q)
+            if (q == hi[i]) {
+                mi[i] = m[q];
+                di[i] = den[q];
+            }
+        acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float4* os = reinterpret_cast<const float4*>(p.part_o);
+    const int64_t row = static_cast<int64_t>(p.G) * D / 4;  // float4 per piece partial
+    for (int k0 = 0; k0 < np; k0 += KB) {
+        float4 ov[KB][IT];
+        float lw[KB][IT];
+#pragma unroll
+        for (int b = 0; b < KB; ++b)
+#pragma unroll
+            for (int i = 0; i < IT; ++i) {
+                const int f = lane + 32 * i;
+                const bool live = f < nf && k0 + b < np;
+                const int64_t k = base + min(k0 + b, np - 1);
+                ov[b][i] = live ? __ldcg(os + k * row + static_cast<int64_t>(h0) * (D / 4) + f)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                lw[b][i] = live ? __ldcg(p.part_lse + k * p.G + h0 + hi[i]) : -INFINITY;
+            }
+#pragma unroll
+        for (int b = 0; b < KB; ++b)
+#pragma unroll
+            for (int i = 0; i < IT; ++i) {
+                const float wgt = ex2(lw[b][i] - mi[i]);
+                acc[i].x += wgt * ov[b][i].x;
+                acc[i].y += wgt * ov[b][i].y;
+                acc[i].z += wgt * ov[b][i].z;
+                acc[i].w += wgt * ov[b][i].w;
+            }
+    }
+    const int64_t head0 = static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G + h0;
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+        const int f = lane + 32 * i;
+        if (f < nf) {
+            const float inv = 1.f / di[i];
+            __half2* d2 = reinterpret_cast<__half2*>(p.out + head0 * D + f * 4);
+            d2[0] = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
+            d2[1] = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
+        }
+    }
+}
+
+// The merge tasks dealt to warp w (w, w + Wtot, ...): each waits, bounded,
+// until its unit's pieces are all counted, merges its heads and publishes them.
 template <int D, int NT>
-__device__ __forceinline__ void merge_pieces(const PlanParams& p, int base, int npieces, int64_t head0, int lane) {
-    constexpr int ITEMS = NT * 8 * D / 128;  // float4 items per lane for G = 8*NT
-    constexpr int ROUND = ITEMS < 8 ? ITEMS : 8;
-    const int nf = p.G * D / 4;
-    const float* lse = p.part_lse + static_cast<int64_t>(base) * p.G;
-    const float4* os = reinterpret_cast<const float4*>(p.part_o + static_cast<int64_t>(base) * p.G * D);
-    for (int i0 = 0; i0 < ITEMS; i0 += ROUND) {
-        float m[ROUND], den[ROUND];
-        float4 acc[ROUND];
-        int h[ROUND];
-#pragma unroll
-        for (int i = 0; i < ROUND; ++i) {
-            m[i] = -INFINITY;
-            den[i] = 0.f;
-            acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            const int f = lane + 32 * (i0 + i);
-            h[i] = f < nf ? (f * 4) / D : 0;
-        }
-        for (int k = 0; k < npieces; ++k) {
-            float l[ROUND];
-            float4 o[ROUND];
-#pragma unroll
-            for (int i = 0; i < ROUND; ++i) {
-                const int f = lane + 32 * (i0 + i);
-                const int fc = f < nf ? f : 0;
-                l[i] = __ldcg(lse + k * p.G + h[i]);
-                o[i] = __ldcg(os + static_cast<int64_t>(k) * nf + fc);
-            }
-#pragma unroll
-            for (int i = 0; i < ROUND; ++i) {
-                const float mn = fmaxf(m[i], l[i]);
-                const float a = ex2(m[i] - mn), b = ex2(l[i] - mn);
-                den[i] = den[i] * a + b;
-                acc[i].x = acc[i].x * a + b * o[i].x;
-                acc[i].y = acc[i].y * a + b * o[i].y;
-                acc[i].z = acc[i].z * a + b * o[i].z;
-                acc[i].w = acc[i].w * a + b * o[i].w;
-                m[i] = mn;
+__device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int Wtot, int lane) {
+    for (int k = w; k < p.ntasks; k += Wtot) {
+        const int u = p.tunits[k / p.S];
+        const int hs = p.G / p.S;
+        const int h0 = (k % p.S) * hs;
+        const int np = p.unp[u];
+        int ok = 1;
+        if (lane == 0) {
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_gpu(&p.counters[u]) < static_cast<unsigned int>(np)) {
+                // give up at once if a piece's warp already gave up on a wait
+                if ((*reinterpret_cast<volatile uint32_t*>(p.err) & VK_ERR_TIMEOUT) ||
+                    global_ns() - t0 > kGatherWaitNs) {
+                    atomicOr(p.err, VK_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(32);
             }
         }
-#pragma unroll
-        for (int i = 0; i < ROUND; ++i) {
-            const int f = lane + 32 * (i0 + i);
-            if (f < nf) {
-                const float inv = 1.f / den[i];
-                __half2* dst = reinterpret_cast<__half2*>(p.out + head0 * D + f * 4);
-                dst[0] = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
-                dst[1] = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
-            }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok) {
+            const int ni = (hs * D / 4 + 31) / 32;  // float4 items per lane
+            if (ni <= 1) merge_task<D, NT, 1>(p, u, h0, hs, np, lane);
+            else if (ni <= 2) merge_task<D, NT, 2>(p, u, h0, hs, np, lane);
+            else if (ni <= 4) merge_task<D, NT, 4>(p, u, h0, hs, np, lane);
+            else if (ni <= 8) merge_task<D, NT, 8>(p, u, h0, hs, np, lane);
+            else merge_task<D, NT, 16>(p, u, h0, hs, np, lane);
         }
+        __syncwarp();
+        if (lane == 0 && atomicAdd(&p.counters[p.U + u], 1u) == static_cast<unsigned int>(p.S - 1)) {
+            p.counters[u] = 0u;  // every task of the unit has passed its wait
+            p.counters[p.U + u] = 0u;
+        }
+        if (ok) publish_heads<D>(p, u, h0, hs, lane);
     }
 }
 
@@ -186,7 +344,12 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     const int n = w < p.W ? p.wb[w + 1] - g0 : 0;
     if (n <= 0) {
         griddep_wait();
-        for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) zero_unit<D>(p, p.zunits[i], lane);
+        wait_prev_slot(p, lane);
+        for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
+            zero_unit<D>(p, p.zunits[i], lane);
+            publish_unit<D>(p, p.zunits[i], lane);
+        }
+        run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
         return;
     }
 
@@ -199,27 +362,48 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     PageIt pf{u0, g0 - p.uoff[u0], p.uoff[u0 + 1] - p.uoff[u0]};  // prefetch cursor
     PageIt cu = pf;                                                // consume cursor
 
-    // Loads page `pf` into stage s (whole warp; lane 0 issues the TMA).
-    auto issue = [&](int s) {
-        const int b = pf.u / p.Hkv, hkv = pf.u % p.Hkv;
-        int page = p.bt[static_cast<int64_t>(b) * p.bt_stride + pf.p];
-        if (page < 0 || page >= p.num_pages) {
-            if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
-            page = 0;
-        } else if (p.k_new != nullptr && pf.p == pf.np - 1) {
-            // fused append of the token at position len-1 into this page
-            const int slot = (p.ulen[pf.u] - 1) % P;
-            char* dk = p.pool_base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
-                       static_cast<uint64_t>(hkv) * p.head_bytes + static_cast<uint64_t>(slot) * D * 2;
-            const int64_t src = (static_cast<int64_t>(b) * p.Hkv + hkv) * D;
-            for (int v = lane; v < 2 * (D / 8); v += 32) {
-                const bool is_v = v >= D / 8;
-                const int vi = is_v ? v - D / 8 : v;
-                const uint4 val = __ldg(reinterpret_cast<const uint4*>((is_v ? p.v_new : p.k_new) + src) + vi);
-                reinterpret_cast<uint4*>(dk + (is_v ? P * D * 2 : 0))[vi] = val;
+    // Block-table entries of the next 32 pages of the range, one per lane, read
+    // in one coalesced round trip instead of one dependent load per page.
+    int nissued = 0;  // pages of the range issued so far
+    int win = -1;     // page id of range page (nissued & ~31) + lane; -1 bad or past the end
+    auto load_window = [&]() {
+        win = -1;
+        if (nissued + lane < n) {
+            PageIt c = pf;
+            int adv = lane;
+            while (adv > 0) {
+                const int left = c.np - 1 - c.p;
+                if (adv <= left) {
+                    c.p += adv;
+                    adv = 0;
+                } else {
+                    adv -= left + 1;
+                    c.p = 0;
+                    do {
+                        ++c.u;
+                        c.np = p.uoff[c.u + 1] - p.uoff[c.u];
+                    } while (c.np == 0);
+                }
             }
-            fence_proxy_async_global();
-            __syncwarp();
+            const int page = p.bt[static_cast<int64_t>(c.u / p.Hkv) * p.bt_stride + c.p];
+            if (page < 0 || page >= p.num_pages) atomicOr(p.err, VK_ERR_PAGE_ID);
+            else win = page;
+        }
+    };
+
+    // Loads page `pf` into stage s (whole warp; lane 0 issues the TMA).  The
+    // page that receives the new token is loaded as it is in memory; the new
+    // rows are patched into the stage when it is consumed.
+    uint32_t bad_stages = 0;  // bit s: stage s holds a stand-in for a bad page id
+    auto issue = [&](int s) {
+        const int hkv = pf.u % p.Hkv;
+        if ((nissued & 31) == 0) load_window();
+        int page = __shfl_sync(0xffffffffu, win, nissued & 31);
+        ++nissued;
+        bad_stages &= ~(1u << s);
+        if (page < 0) {
+            page = 0;  // recorded in the error word; read a valid page instead
+            bad_stages |= 1u << s;
         }
         if (lane == 0) {
             const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
@@ -232,13 +416,17 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
         pf.next(p.uoff);
     };
 
-    // Prefetch the first stages; a unit's last page waits for k_new/v_new.
+    // Prefetch the first stages (block tables and pages only: nothing the
+    // preceding kernel writes).
     const int pre = min(n, NS);
     int issued = 0;
-    while (issued < pre && !(p.k_new != nullptr && pf.p == pf.np - 1)) issue(issued++);
-    griddep_wait();
     while (issued < pre) issue(issued++);
-    for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) zero_unit<D>(p, p.zunits[i], lane);
+    griddep_wait();
+    wait_prev_slot(p, lane);
+    for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
+        zero_unit<D>(p, p.zunits[i], lane);
+        publish_unit<D>(p, p.zunits[i], lane);
+    }
 
     uint32_t qf[NT][KS][2];
     WarpSoftmaxState<D, NT> st;
@@ -247,12 +435,55 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
 
     for (int j = 0; j < n; ++j) {
         const int s = j % NS;
+        // Fused append: the unit's last page takes the new token at slot
+        // (len-1) % P; its K and V rows are read now (in flight during the
+        // stage wait), stored to the pool and patched into the stage.
+        const bool app = p.k_new != nullptr && cu.p == cu.np - 1 && !((bad_stages >> s) & 1u);
+        constexpr int NCH = D / 8;  // 16-byte chunks per row
+        uint4 row_val[(2 * NCH + 31) / 32];
+        int app_page = 0, app_slot = 0;
+        if (app) {
+            const int b = cu.u / p.Hkv, hkv = cu.u % p.Hkv;
+            app_page = p.bt[static_cast<int64_t>(b) * p.bt_stride + cu.p];
+            app_slot = (p.ulen[cu.u] - 1) % P;
+            const int64_t src = (static_cast<int64_t>(b) * p.Hkv + hkv) * D;
+#pragma unroll
+            for (int i = 0; i < (2 * NCH + 31) / 32; ++i) {
+                const int v = lane + 32 * i;
+                const bool is_v = v >= NCH;
+                row_val[i] = v < 2 * NCH ? __ldg(reinterpret_cast<const uint4*>((is_v ? p.v_new : p.k_new) + src) +
+                                                 (is_v ? v - NCH : v))
+                                         : make_uint4(0, 0, 0, 0);
+            }
+        }
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), (j / NS) & 1, p.err))) return;
+        if (app) {
+            const int hkv = cu.u % p.Hkv;
+            char* dk = p.pool_base + p.layer_off + static_cast<uint64_t>(app_page) * p.seg_bytes +
+                       static_cast<uint64_t>(hkv) * p.head_bytes + static_cast<uint64_t>(app_slot) * D * 2;
+            const uint32_t sb = smem_u32(my_stages + s * SB);
+#pragma unroll
+            for (int i = 0; i < (2 * NCH + 31) / 32; ++i) {
+                const int v = lane + 32 * i;
+                if (v < 2 * NCH) {
+                    const bool is_v = v >= NCH;
+                    const int vi = is_v ? v - NCH : v;
+                    reinterpret_cast<uint4*>(dk + (is_v ? P * D * 2 : 0))[vi] = row_val[i];
+                    const int r = (is_v ? P : 0) + app_slot, d0 = vi * 8;
+                    const uint32_t a = sb + (d0 >> 6) * (2 * P * 128) + swz128(r, (d0 & 63) >> 3);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(row_val[i].x),
+                                 "r"(row_val[i].y), "r"(row_val[i].z), "r"(row_val[i].w)
+                                 : "memory");
+                }
+            }
+            __syncwarp();
+        }
         const int valid = min(P, p.ulen[cu.u] - cu.p * P);
         page_update<D, NT>(smem_u32(my_stages + s * SB), valid, qf, st, p.scale_log2, lane);
         // Every lane's ldmatrix results for stage s have been consumed by its MMAs
         // before __syncwarp returns, so the stage can be refilled.
         __syncwarp();
+        if (app) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // patch before the next TMA write
         if (j + NS < n) issue(s);
 
         const bool unit_done = (cu.p == cu.np - 1) || (j == n - 1);
@@ -280,9 +511,9 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                         }
                     }
                 }
+                publish_unit<D>(p, u, lane);
             } else {
-                const int base = p.uslot[u];
-                const int slot = base + (w - p.ufw[u]);
+                const int slot = p.uslot[u] + (w - p.ufw[u]);
                 float* po = p.part_o + static_cast<int64_t>(slot) * p.G * D;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
@@ -305,16 +536,8 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                         if (h0 + 1 < p.G) p.part_lse[static_cast<int64_t>(slot) * p.G + h0 + 1] = st.m[nt][1] + __log2f(st.l[nt][1]);
                     }
                 }
-                __threadfence();
-                __syncwarp();
-                unsigned int prev = 0;
-                if (lane == 0) prev = atomicAdd(&p.counters[u], 1u);
-                prev = __shfl_sync(0xffffffffu, prev, 0);
-                if (prev == static_cast<unsigned int>(npieces - 1)) {
-                    __threadfence();
-                    merge_pieces<D, NT>(p, base, npieces, head0, lane);
-                    if (lane == 0) atomicExch(&p.counters[u], 0u);
-                }
+                __syncwarp();  // every lane's partial stores precede lane 0's release
+                if (lane == 0) atom_add_release_gpu(&p.counters[u], 1u);
             }
             if (j + 1 < n) {
                 cu.next(p.uoff);
@@ -326,6 +549,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             cu.next(p.uoff);
         }
     }
+    run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
 }
 
 template <int D, int NT>
@@ -362,9 +586,13 @@ struct vk_decode_plan {
     int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1;
     int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
     std::vector<int32_t> tables;
-    size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_z = 0;
+    size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
+    int ntasks = 0, S = 1, ndone = 0;
     size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
     bool early_start = false;
+    vk_gather* gather = nullptr;
+    int gather_slot_base = 0;
+    bool gather_wait_prev = false;
 };
 
 using namespace vk;
@@ -424,7 +652,8 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
             return fail(VK_CUDA_ERROR, "occupancy query for the planned decode kernel failed");
         }
     }
-    const int64_t cap = static_cast<int64_t>(pool->num_sms) * occ * kPlanWarps;
+    int64_t cap = static_cast<int64_t>(pool->num_sms) * occ * kPlanWarps;
+    if (pool->plan_workers > 0) cap = std::min<int64_t>(cap, pool->plan_workers);
     int64_t W = T > 0 ? std::min<int64_t>(cap, (T + kMinPagesPerWorker - 1) / kMinPagesPerWorker) : 0;
     W = std::max<int64_t>(W, T > 0 ? 1 : 0);
     pl->W = static_cast<int>(W);
@@ -443,7 +672,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         }
     }
     // pieces per unit
-    std::vector<int32_t> ufw(U, 0), unp(U, 0), uslot(U, -1);
+    std::vector<int32_t> ufw(U, 0), unp(U, 0), uslot(U, -1), tunits;
     auto worker_of = [&](int64_t g) {  // largest w with wb[w] <= g
         int64_t lo = 0, hi = W - 1;
         while (lo < hi) {
@@ -461,9 +690,21 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         if (unp[u] > 1) {
             uslot[u] = slots;
             slots += unp[u];
+            tunits.push_back(u);
         }
     }
     pl->slots = slots;
+    // merge tasks: each split unit's G query heads in S groups, S as large as
+    // the grid's warps allow (a power of two dividing G)
+    {
+        const int64_t nmulti = static_cast<int64_t>(tunits.size());
+        const int64_t wtot = static_cast<int64_t>(pl->grid) * kPlanWarps;
+        int S = 1;
+        while (S * 2 <= G && G % (S * 2) == 0 && nmulti * S * 2 <= wtot) S *= 2;
+        pl->S = S;
+        pl->ntasks = static_cast<int>(nmulti * S);
+        pl->ndone = U + static_cast<int>(nmulti) * (S - 1);
+    }
 
     // packed int32 tables
     auto& t = pl->tables;
@@ -481,10 +722,11 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     put(ufw, &pl->o_ufw);
     put(unp, &pl->o_unp);
     put(uslot, &pl->o_uslot);
+    put(tunits, &pl->o_tu);
     put(zunits, &pl->o_z);
     pl->tables_bytes = t.size() * sizeof(int32_t);
     pl->counters_off = align256(pl->tables_bytes);
-    pl->part_o_off = align256(pl->counters_off + static_cast<size_t>(U) * sizeof(uint32_t));
+    pl->part_o_off = align256(pl->counters_off + static_cast<size_t>(2 * U) * sizeof(uint32_t));
     pl->part_lse_off = align256(pl->part_o_off + static_cast<size_t>(slots) * G * D * sizeof(float));
     pl->ws_bytes = align256(pl->part_lse_off + static_cast<size_t>(slots) * G * sizeof(float));
     *out_plan = pl;
@@ -508,7 +750,7 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, siz
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(plan tables)");
     if (plan->U > 0) {
         e = cudaMemsetAsync(static_cast<char*>(workspace) + plan->counters_off, 0,
-                            static_cast<size_t>(plan->U) * sizeof(uint32_t), st);
+                            static_cast<size_t>(2 * plan->U) * sizeof(uint32_t), st);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(plan counters)");
     }
     return VK_OK;
@@ -517,6 +759,28 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, siz
 vk_status vk_decode_plan_set_early_start(vk_decode_plan* plan, int32_t enable) {
     if (!plan) return fail(VK_INVALID_ARG, "plan is NULL");
     plan->early_start = enable != 0;
+    return VK_OK;
+}
+
+vk_status vk_set_decode_workers(vk_pool* pool, int32_t max_workers) {
+    if (!pool || max_workers < 0) return fail(VK_INVALID_ARG, "pool NULL or negative worker cap");
+    pool->plan_workers = max_workers;
+    return VK_OK;
+}
+
+vk_status vk_decode_plan_set_gather(vk_decode_plan* plan, vk_gather* g, int32_t slot_base, int32_t wait_prev) {
+    if (!plan) return fail(VK_INVALID_ARG, "plan is NULL");
+    if (slot_base < 0) return fail(VK_INVALID_ARG, "negative slot_base");
+    if (g) {
+        GatherView v;
+        if (!gather_view(g, &v)) return fail(VK_INVALID_ARG, "gather has peers not imported");
+        if (gather_device(g) != plan->device) return fail(VK_INVALID_ARG, "gather lives on another device");
+        const uint64_t need = static_cast<uint64_t>(plan->B) * plan->Hq * plan->D * 2;
+        if (v.slice_bytes < need) return fail(VK_INVALID_ARG, "gather slice smaller than the plan's [B, Hq, D] output");
+    }
+    plan->gather = g;
+    plan->gather_slot_base = slot_base;
+    plan->gather_wait_prev = g && wait_prev != 0;
     return VK_OK;
 }
 
@@ -541,7 +805,18 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
         return fail(VK_INVALID_ARG, "plan was made for another pool shape or device");
     if (layer < 0 || layer >= pool->cfg.num_layers) return fail(VK_INVALID_ARG, "layer out of range");
     if (plan->B == 0) return VK_OK;
-    if (!q || !out || !block_tables || !workspace) return fail(VK_INVALID_ARG, "NULL array");
+    GatherView gv{};
+    if (plan->gather) {
+        if (!gather_view(plan->gather, &gv)) return fail(VK_INVALID_ARG, "gather has peers not imported");
+        if (out && (reinterpret_cast<uintptr_t>(out) & 15)) return fail(VK_INVALID_ARG, "out must be 16-byte aligned with a gather");
+    } else if (!out) {
+        return fail(VK_INVALID_ARG, "NULL out");
+    }
+    const int gslot = plan->gather ? (plan->gather_slot_base + layer) % gv.slots : -1;
+    const bool out_own = plan->gather && !out;
+    if (out_own) out = gv.base[gv.rank] + static_cast<uint64_t>(gslot) * gv.slot_bytes +
+                       static_cast<uint64_t>(gv.rank) * gv.slice_bytes;
+    if (!q || !block_tables || !workspace) return fail(VK_INVALID_ARG, "NULL array");
     if (bt_stride < plan->max_unit_pages) return fail(VK_INVALID_ARG, "block table narrower than the longest sequence");
     if ((k_new == nullptr) != (v_new == nullptr)) return fail(VK_INVALID_ARG, "give both k_new and v_new or neither");
     if (k_new && ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15))
@@ -560,6 +835,10 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.ufw = t + plan->o_ufw;
     p.unp = t + plan->o_unp;
     p.uslot = t + plan->o_uslot;
+    p.tunits = t + plan->o_tu;
+    p.ntasks = plan->ntasks;
+    p.S = plan->S;
+    p.ndone = plan->ndone;
     p.zunits = t + plan->o_z;
     p.counters = reinterpret_cast<uint32_t*>(ws + plan->counters_off);
     p.part_o = reinterpret_cast<float*>(ws + plan->part_o_off);
@@ -583,6 +862,11 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.num_pages = pool->num_pages;
     p.W = plan->W;
     p.Z = plan->Z;
+    p.U = plan->U;
+    p.g = gv;
+    p.gslot = gslot;
+    p.gwait_slot = plan->gather_wait_prev ? (gslot + gv.slots - 1) % gv.slots : -1;
+    p.out_own = out_own ? 1 : 0;
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;
     if (plan->grid <= 0) return VK_OK;

@@ -1,0 +1,62 @@
+// Device helpers of the fused head-shard output gather: system-scope flag
+// loads and stores over NVLink and a bounded wait on one slot's flags.
+#pragma once
+
+#include "vk_internal.h"
+
+namespace vk {
+
+constexpr uint64_t kGatherWaitNs = 1000000000ull;  // 1 s bound on a cross-GPU wait
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t* gather_flag(const GatherView& g, int on_rank, int slot, int from_rank) {
+    return reinterpret_cast<uint32_t*>(g.base[on_rank] + g.flags_off) + slot * g.world + from_rank;
+}
+
+// One thread: waits until every rank's flag of `slot` in this rank's block has
+// reached this rank's own flag (the count of layers this rank has published in
+// the slot).  Flags only grow (mod 2^32).  False, with VK_ERR_TIMEOUT, after
+// kGatherWaitNs.
+__device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, uint32_t* err) {
+    const uint32_t target = ld_acquire_sys(gather_flag(g, g.rank, slot, g.rank));
+    const uint64_t t0 = global_ns();
+    for (int r = 0; r < g.world; ++r) {
+        const uint32_t* f = gather_flag(g, g.rank, slot, r);
+        while (static_cast<int32_t>(ld_acquire_sys(f) - target) < 0) {
+            if (global_ns() - t0 > kGatherWaitNs) {
+                atomicOr(err, VK_ERR_TIMEOUT);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+// After every unit of a layer has been stored into all ranks' slices: called by
+// the one thread that counted the last unit.  Raises this rank's flag of
+// `slot` on every rank (own included) to its next value.
+__device__ __forceinline__ void gather_signal(const GatherView& g, int slot) {
+    __threadfence_system();
+    const uint32_t next = *reinterpret_cast<volatile uint32_t*>(gather_flag(g, g.rank, slot, g.rank)) + 1u;
+    for (int r = 0; r < g.world; ++r)
+        if (r != g.rank) st_release_sys(gather_flag(g, r, slot, g.rank), next);
+    st_release_sys(gather_flag(g, g.rank, slot, g.rank), next);
+}
+
+}  // namespace vk

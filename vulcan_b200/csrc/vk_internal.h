@@ -52,6 +52,7 @@ struct vk_pool {
     bool tmap_ok = false;
     int32_t prefill_path = 0;        // 0 auto, 1 mma.sync kernel, 2 tcgen05 kernel
     int32_t split_override = 0;
+    int32_t plan_workers = 0;        // cap on planned-decode workers (0 = resident warps)
     int32_t num_sms = vk::kNumSmsDefault;
     vk::Allocator alloc;
 };
@@ -84,6 +85,20 @@ vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* ds
 vk_status launch_remap(int32_t* bt, int64_t entries, const int32_t* map, int map_len,
                        cudaStream_t st);
 int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len);
+
+// Device-side description of a bound output gather (vk_gather), passed by value
+// in kernel parameters.  Allocation of every rank: [slots][world][slice] fp16
+// receive slices, then flags [slots][world] u32 (written only by the rank of
+// the column), then done counters [slots] u32 (local).
+constexpr int kMaxGatherRanks = 8;
+struct GatherView {
+    char* base[kMaxGatherRanks];  // receive allocations of all ranks, own included
+    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, done_off = 0;
+    int rank = 0, world = 0, slots = 0;
+};
+// Fills `v` if every peer is imported; false otherwise.
+bool gather_view(const vk_gather* g, GatherView* v);
+int gather_device(const vk_gather* g);
 vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const int32_t* bt, int bt_stride,
                      const int32_t* positions, int B, int T, int Hq, float scale, cudaStream_t st);
 

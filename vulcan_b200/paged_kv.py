@@ -169,6 +169,10 @@ class PagedKVPool:
     def set_split(self, pages_per_split: int) -> None:
         check(self._lib.vk_set_decode_split(self.handle, pages_per_split), "vk_set_decode_split")
 
+    def set_plan_workers(self, max_workers: int) -> None:
+        """Caps the workers of plans made afterwards (0 = one per resident warp)."""
+        check(self._lib.vk_set_decode_workers(self.handle, max_workers), "vk_set_decode_workers")
+
     def workspace(self, batch: int, num_q_heads: int, max_seq_len: int) -> Optional[torch.Tensor]:
         need = self.workspace_size(batch, num_q_heads, max_seq_len)
         if need == 0:
@@ -288,6 +292,15 @@ class DecodePlan:
         check(self._lib.vk_decode_plan_set_early_start(self.handle, int(bool(enable))),
               "vk_decode_plan_set_early_start")
 
+    def set_gather(self, gather: Optional["Gather"], slot_base: int = 0, wait_prev: bool = True) -> None:
+        """Binds a fused output gather (see Gather); a run of layer l then writes
+        every rank's receive slice of slot ``(slot_base + l) % slots`` and may
+        leave ``out`` as None.  ``wait_prev``: wait for the previous slot first."""
+        check(self._lib.vk_decode_plan_set_gather(self.handle, gather.handle if gather else None,
+                                                  int(slot_base), int(bool(wait_prev))),
+              "vk_decode_plan_set_gather")
+        self.gather = gather
+
     @property
     def workers(self) -> int:
         return self.info(0)
@@ -312,7 +325,7 @@ class DecodePlan:
         if k_new is not None:
             _need(k_new, torch.float16, "k_new")
             _need(v_new, torch.float16, "v_new")
-        if out is None:
+        if out is None and getattr(self, "gather", None) is None:
             out = torch.empty_like(q)
         check(self._lib.vk_decode_run(self.pool.handle, self.handle, layer, _ptr(q), _ptr(out), _ptr(block_tables),
                                       block_tables.shape[1], _ptr(k_new), _ptr(v_new), float(scale),
@@ -327,6 +340,95 @@ class DecodePlan:
     def __del__(self):
         try:
             self.close()
+        except Exception:
+            pass
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over library-owned device memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+class Gather:
+    """vk_gather: head-sharded output all-gather fused into the planned decode.
+
+    Each rank creates one with the same ``slice_bytes`` (its [B, Hq/world, D]
+    fp16 output) and ``slots``; the ranks then swap ``export()`` handles over
+    any host transport (``exchange`` does it with torch.distributed) and
+    ``import_peer`` every other rank's.  ``view(slot, B, Hq_local, D)`` is the
+    rank's receive buffer of a slot as [world, B, Hq_local, D] fp16."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rank: int, world: int, slice_bytes: int, slots: int, device=None):
+        self._lib = _lib.load()
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                           (device.index if isinstance(device, torch.device) else int(device)))
+        self.device, self.rank, self.world, self.slots, self.slice_bytes = dev, rank, world, slots, slice_bytes
+        h = ctypes.c_void_p()
+        check(self._lib.vk_gather_create(dev.index, rank, world, slice_bytes, slots, ctypes.byref(h)),
+              "vk_gather_create")
+        self.handle = h
+
+    def export(self) -> bytes:
+        buf = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        check(self._lib.vk_gather_export(self.handle, buf), "vk_gather_export")
+        return buf.raw
+
+    def import_peer(self, peer: int, handle: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(handle), self.HANDLE_BYTES)
+        check(self._lib.vk_gather_import(self.handle, peer, buf), "vk_gather_import")
+
+    def exchange(self, group=None) -> None:
+        """Swaps handles with every rank through torch.distributed (host side)."""
+        import torch.distributed as dist
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.export(), group=group)
+        for r, hd in enumerate(handles):
+            if r != self.rank:
+                self.import_peer(r, hd)
+
+    def buffer_ptr(self, slot: int) -> int:
+        p = self._lib.vk_gather_buffer(self.handle, slot)
+        if not p:
+            raise VKError(1, "vk_gather_buffer")
+        return p
+
+    def view(self, slot: int, batch: int, heads_local: int, head_dim: int) -> torch.Tensor:
+        n = self.world * batch * heads_local * head_dim
+        if n * 2 > self.world * self.slice_bytes:
+            raise ValueError("view larger than the slot")
+        arr = _DeviceArray(self.buffer_ptr(slot), (self.world, batch, heads_local, head_dim), "<f2")
+        return torch.as_tensor(arr, device=self.device)
+
+    def wait(self, slot: int, stream=None) -> None:
+        check(self._lib.vk_gather_wait(self.handle, slot, _stream(stream)), "vk_gather_wait")
+
+    def check(self) -> None:
+        check(self._lib.vk_gather_check(self.handle), "vk_gather_check")
+
+    def release_peers(self) -> None:
+        check(self._lib.vk_gather_release_peers(self.handle), "vk_gather_release_peers")
+
+    def close(self, group=None) -> None:
+        """Two-phase teardown: release the peer mappings, meet every rank at a
+        torch.distributed barrier (when world > 1), then free the buffer."""
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            if self.world > 1:
+                import torch.distributed as dist
+                self.release_peers()
+                dist.barrier(group=group)
+            self._lib.vk_gather_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            if getattr(self, "handle", None) is not None and self.handle.value:
+                self._lib.vk_gather_destroy(self.handle)
+                self.handle = ctypes.c_void_p()
         except Exception:
             pass
 
