@@ -383,7 +383,7 @@ def main():
         if gathered is not None:
             cur.wait_stream(comm)
         if gat is not None:
-            gat.wait(L - 1)  # the last layer's slices from every rank
+            plan.gather_wait(L - 1)  # signal the last layer's slot, wait for every rank's
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -853,7 +853,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
                 # (a bounded flag wait on peers' stores), then reads the slot
                 d2h.wait_event(fe)
                 with torch.cuda.stream(d2h):
-                    gat.wait(base + l, stream=d2h)
+                    plan.gather_wait(l, stream=d2h)
                     hout[l].copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
             elif gathered_host:
                 comm.wait_event(fe)

@@ -214,10 +214,10 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
  * KV-head sharding over `world` GPUs of one node (one process per GPU): rank r
  * owns a contiguous block of KV heads and their query heads, and every rank
  * needs the whole [B, Hq, D] output of each layer.  Instead of a separate
- * collective, the planned decode bound to a gather writes each finished
- * (sequence, KV head) output straight into every rank's receive buffer with
- * peer stores over NVLink, and when its last unit of the layer is out it raises
- * this rank's flag in every rank's flag block.  No multicast is used.
+ * collective, the planned decode bound to a gather stores each finished output
+ * straight into every rank's receive buffer over NVLink (plain peer stores, no
+ * multicast), and the next run on the stream, which starts only once this one
+ * has completed, raises this rank's flag of the slot on every rank.
  *
  * Receive buffer of each rank: `slots` slots of [world][slice_bytes]; rank r's
  * slice of a slot holds its [B, Hq/world, D] fp16 output of one layer (the
@@ -226,22 +226,31 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
  *   vk_gather_export(g, handle)            VK_GATHER_HANDLE_BYTES opaque bytes
  *   ... exchange handles between the ranks (any host transport) ...
  *   vk_gather_import(g, peer, peer_handle) for every peer != rank
+ * Per step of L layers (same plan, one stream):
  *   vk_decode_plan_set_gather(plan, g, slot_base, wait_prev)
- * A run of layer l writes slot (slot_base + l) % slots.  With a gather bound,
- * vk_decode_run's `out` may be NULL (the rank's own slice of the slot is
- * written), else it must be 16-byte aligned and is written as well.  With
- * wait_prev = 1, every run first waits (bounded, 1 s; VK_ERR_TIMEOUT on
- * expiry) until all ranks' slices of the slot before its own have arrived,
- * before it reads q, k_new or v_new: the order of a model whose next layer
- * consumes the gathered output.  With wait_prev = 0 the gather of layer l
- * overlaps layer l+1 (the order of an all-gather on a side stream), and
- * vk_gather_wait makes a stream wait for one slot; since each rank raises its
- * flags in layer order, waiting for the slot of a step's last layer covers the
- * step.  The library does not order a slot's reuse against the readers of a
- * receive buffer: callers rewrite a slot only after a wait that follows its
- * readers on every rank (for example slot_base 0 and L on alternate steps of
- * L layers, with 2L slots).  No reference counterpart: the reference runs on
- * one GPU. */
+ *   vk_decode_plan_upload(...)                       starts a new step epoch
+ *   vk_decode_run(layer 0), ..., vk_decode_run(layer L-1)
+ *   vk_decode_plan_gather_wait(plan, ws, L-1, stream)
+ * Run l writes slot (slot_base + l) % slots; run l > 0 raises the flags of run
+ * l-1's slot, so the runs of a step must be issued in layer order on one
+ * stream (other kernels may sit between them).  vk_decode_plan_gather_wait
+ * raises the flags of its layer's slot (its run must precede it on the stream)
+ * and makes the stream wait until all ranks' slices of that slot have arrived;
+ * since every rank signals its slots in layer order, the wait on the last
+ * layer covers the whole step.  With a gather bound, vk_decode_run's `out` may
+ * be NULL (the rank's own slice of the slot is written), else it must be
+ * 16-byte aligned and is written as well.  With wait_prev = 1, every run of a
+ * layer l > 0 waits before it reads q, k_new or v_new until all ranks' slices
+ * of layer l-1's slot have arrived (layer 0 follows the previous step's
+ * vk_decode_plan_gather_wait): the order of a model whose next layer consumes
+ * the gathered output; with wait_prev = 0 the gather of layer l overlaps layer l+1
+ * (the order of an all-gather on a side stream).  Waits are bounded (1 s) and
+ * record VK_ERR_TIMEOUT (vk_pool_check for runs, vk_gather_check for
+ * vk_decode_plan_gather_wait).  The library does not order a slot's reuse
+ * against the readers of a receive buffer: callers rewrite a slot only after a
+ * wait that follows its readers on every rank (for example slot_base 0 and L
+ * on alternate steps of L layers, with 2L slots).  No reference counterpart:
+ * the reference runs on one GPU. */
 #define VK_GATHER_HANDLE_BYTES 64
 typedef struct vk_gather vk_gather;
 
@@ -257,14 +266,15 @@ vk_status vk_gather_export(const vk_gather* g, void* handle_out);
 vk_status vk_gather_import(vk_gather* g, int32_t peer, const void* handle);
 /* This rank's receive buffer of one slot: [world][slice_bytes] (NULL if bad). */
 void*     vk_gather_buffer(const vk_gather* g, int32_t slot);
-vk_status vk_gather_wait(vk_gather* g, int32_t slot, void* stream);
-/* Synchronous: VK_TIMEOUT if a vk_gather_wait gave up since the last check
- * (timeouts inside vk_decode_run are reported by vk_pool_check). */
+/* Synchronous: VK_TIMEOUT if a vk_decode_plan_gather_wait gave up since the
+ * last check (timeouts inside vk_decode_run are reported by vk_pool_check). */
 vk_status vk_gather_check(vk_gather* g);
 /* Binds (g != NULL) or unbinds (g == NULL) a gather; slice_bytes must cover
  * the plan's [B, Hq, D] fp16 output, and every peer must be imported. */
 vk_status vk_decode_plan_set_gather(vk_decode_plan* plan, vk_gather* g, int32_t slot_base,
                                     int32_t wait_prev);
+vk_status vk_decode_plan_gather_wait(const vk_decode_plan* plan, void* workspace, int32_t layer,
+                                     void* stream);
 
 /* ---- K3: chunked prefill -------------------------------------------------
  * The prefill use of launch_attention (src/transformer.cpp:136-189 with

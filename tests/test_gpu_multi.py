@@ -81,7 +81,7 @@ def _worker(rank, world, port, results):
         gplan.run(0, qd, bt_d)
         gplan.run(1, qd, bt_d, k_new=torch.from_numpy(np.ascontiguousarray(kn[:, sh.kv_lo:sh.kv_hi])).to(dev),
                   v_new=torch.from_numpy(np.ascontiguousarray(vn[:, sh.kv_lo:sh.kv_hi])).to(dev))
-        gat.wait(1)
+        gplan.gather_wait(1)
         fused = gat.view(1, B, sh.num_q_heads, g.D)
         torch.cuda.synchronize()
         gat.check()

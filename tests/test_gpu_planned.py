@@ -147,7 +147,7 @@ def test_planned_fused_gather_one_rank(vk):
             r = gplan.run(l, dev_f16(q), bt_d, out=explicit)
             if explicit is not None:
                 assert torch.equal(r, plain[l])
-        gat.wait(base + L - 1)
+        gplan.gather_wait(L - 1)
         for l in range(L):
             assert torch.equal(gat.view(base + l, B, Hq, D)[0], plain[l]), "step %d layer %d" % (step, l)
         gplan.set_gather(None)

@@ -68,7 +68,7 @@ SIGNATURES = {
     "vk_gather_export": (c_i32, [vp, vp]),
     "vk_gather_import": (c_i32, [vp, c_i32, vp]),
     "vk_gather_buffer": (vp, [vp, c_i32]),
-    "vk_gather_wait": (c_i32, [vp, c_i32, vp]),
+    "vk_decode_plan_gather_wait": (c_i32, [vp, vp, c_i32, vp]),
     "vk_gather_check": (c_i32, [vp]),
     "vk_decode_plan_set_gather": (c_i32, [vp, vp, c_i32, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),

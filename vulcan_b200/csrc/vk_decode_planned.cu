@@ -65,11 +65,12 @@ struct PlanParams {
     uint64_t seg_bytes, layer_off, head_bytes;
     int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z, U;
     int ntasks, S;   // merge tasks, tasks (head groups) per split unit
-    int ndone;       // units + extra tasks: completions that make a layer's output whole
     float scale_log2;
     // fused output gather (g.world == 0: none)
     GatherView g;
+    const uint32_t* gepoch;  // step epoch of the uploaded plan (flag value)
     int gslot;       // slot this layer writes
+    int gsig_slot;   // slot of the preceding run (its stores are complete): signal it (-1: none)
     int gwait_slot;  // slot to wait for before reading inputs (-1: none)
     int out_own;     // out is this rank's own slice (skip the local copy)
 };
@@ -112,8 +113,8 @@ __device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, un
 
 // Fused gather: the warp that finished `nh` query heads of unit u starting at
 // head h (their [nh, D] outputs are in p.out) copies them in 16-byte pieces
-// into every rank's receive slice, then counts the completion; the warp
-// counting the layer's last completion raises this rank's flag.
+// into every rank's receive slice.  No fence: the slot is signalled by the
+// next run on the stream, once this grid has completed.
 template <int D>
 __device__ __forceinline__ void publish_heads(const PlanParams& p, int u, int h, int nh, int lane) {
     if (p.g.world == 0) return;
@@ -130,18 +131,6 @@ __device__ __forceinline__ void publish_heads(const PlanParams& p, int u, int h,
             reinterpret_cast<uint4*>(p.g.base[r] + off)[c] = v;
         }
     }
-    // __syncwarp orders every lane's peer stores before lane 0's release; the
-    // last completion acquires them all and releases them to the peers with
-    // the flag (one system-scope fence per layer instead of one per warp).
-    __syncwarp();
-    if (lane == 0) {
-        uint32_t* done = reinterpret_cast<uint32_t*>(p.g.base[p.g.rank] + p.g.done_off) + p.gslot;
-        if (atom_add_acq_rel_gpu(done, 1u) == static_cast<uint32_t>(p.ndone - 1)) {
-            *done = 0u;  // every completion of this layer is counted
-            gather_signal(p.g, p.gslot);
-        }
-    }
-    __syncwarp();
 }
 
 template <int D>
@@ -149,10 +138,15 @@ __device__ __forceinline__ void publish_unit(const PlanParams& p, int u, int lan
     publish_heads<D>(p, u, 0, p.G, lane);
 }
 
-// Fused gather: waits until the previous layer's slot is complete on this rank.
-__device__ __forceinline__ void wait_prev_slot(const PlanParams& p, int lane) {
+// Fused gather, after griddepcontrol.wait: warp 0 raises this rank's flags for
+// the preceding run's slot; then (strict order) every warp waits until all
+// ranks' slices of the previous slot have arrived.
+__device__ __forceinline__ void gather_prologue(const PlanParams& p, int w, int lane) {
+    if (p.g.world == 0) return;
+    const uint32_t epoch = *p.gepoch;
+    if (w == 0 && lane == 0 && p.gsig_slot >= 0) gather_signal(p.g, p.gsig_slot, epoch);
     if (p.gwait_slot < 0) return;
-    if (lane == 0) gather_wait_slot(p.g, p.gwait_slot, p.err);
+    if (lane == 0) gather_wait_slot(p.g, p.gwait_slot, epoch, p.err);
     __syncwarp();
 }
 
@@ -266,9 +260,18 @@ __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, i
         const int f = lane + 32 * i;
         if (f < nf) {
             const float inv = 1.f / di[i];
-            __half2* d2 = reinterpret_cast<__half2*>(p.out + head0 * D + f * 4);
-            d2[0] = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
-            d2[1] = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
+            const __half2 lo = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
+            const __half2 hi = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
+            uint2 v;
+            v.x = *reinterpret_cast<const uint32_t*>(&lo);
+            v.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(p.out + head0 * D + f * 4) = v;
+            // fused gather: the same 8 bytes into every rank's receive slice
+            const uint64_t off = static_cast<uint64_t>(p.gslot) * p.g.slot_bytes +
+                                 static_cast<uint64_t>(p.g.rank) * p.g.slice_bytes +
+                                 (static_cast<uint64_t>(head0) * D + f * 4) * 2;
+            for (int r = 0; r < p.g.world; ++r)
+                if (!(r == p.g.rank && p.out_own)) *reinterpret_cast<uint2*>(p.g.base[r] + off) = v;
         }
     }
 }
@@ -310,7 +313,6 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
             p.counters[u] = 0u;  // every task of the unit has passed its wait
             p.counters[p.U + u] = 0u;
         }
-        if (ok) publish_heads<D>(p, u, h0, hs, lane);
     }
 }
 
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     const int n = w < p.W ? p.wb[w + 1] - g0 : 0;
     if (n <= 0) {
         griddep_wait();
-        wait_prev_slot(p, lane);
+        gather_prologue(p, w, lane);
         for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
             zero_unit<D>(p, p.zunits[i], lane);
             publish_unit<D>(p, p.zunits[i], lane);
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     int issued = 0;
     while (issued < pre) issue(issued++);
     griddep_wait();
-    wait_prev_slot(p, lane);
+    gather_prologue(p, w, lane);
     for (int i = w; i < p.Z; i += gridDim.x * kPlanWarps) {
         zero_unit<D>(p, p.zunits[i], lane);
         publish_unit<D>(p, p.zunits[i], lane);
@@ -552,6 +554,16 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
 }
 
+// Signals this rank's stores of `slot` (the preceding run on the stream has
+// completed) and waits until every rank's have arrived.
+__global__ void plan_gather_wait_kernel(const GatherView g, int slot, const uint32_t* epoch_p, uint32_t* err) {
+    if (threadIdx.x == 0) {
+        const uint32_t epoch = *epoch_p;
+        gather_signal(g, slot, epoch);
+        gather_wait_slot(g, slot, epoch, err);
+    }
+}
+
 template <int D, int NT>
 static int plan_occupancy(int device, int* occ_out) {
     static int cache[64] = {};
@@ -585,9 +597,10 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct vk_decode_plan {
     int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1;
     int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
-    std::vector<int32_t> tables;
+    mutable std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
-    int ntasks = 0, S = 1, ndone = 0;
+    int ntasks = 0, S = 1;
+    size_t o_hdr = 0;  // [0]: step epoch written at upload (fused gather)
     size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
     bool early_start = false;
     vk_gather* gather = nullptr;
@@ -703,7 +716,6 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         while (S * 2 <= G && G % (S * 2) == 0 && nmulti * S * 2 <= wtot) S *= 2;
         pl->S = S;
         pl->ntasks = static_cast<int>(nmulti * S);
-        pl->ndone = U + static_cast<int>(nmulti) * (S - 1);
     }
 
     // packed int32 tables
@@ -713,6 +725,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         for (auto x : v) t.push_back(static_cast<int32_t>(x));
         while (t.size() % 64) t.push_back(0);  // keep each array 256-byte aligned
     };
+    put(std::vector<int32_t>{0}, &pl->o_hdr);
     put(wb, &pl->o_wb);
     put(wfu, &pl->o_wfu);
     std::vector<int32_t> uoff32(uoff.begin(), uoff.end());
@@ -746,6 +759,8 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, siz
         return fail(VK_INVALID_ARG, "workspace missing, too small or not 256-byte aligned");
     DeviceGuard g(plan->device);
     cudaStream_t st = as_stream(stream);
+    // each upload with a gather bound starts a new step epoch (flag value)
+    if (plan->gather) plan->tables[plan->o_hdr] = static_cast<int32_t>(gather_next_epoch(plan->gather));
     cudaError_t e = cudaMemcpyAsync(workspace, plan->tables.data(), plan->tables_bytes, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(plan tables)");
     if (plan->U > 0) {
@@ -782,6 +797,20 @@ vk_status vk_decode_plan_set_gather(vk_decode_plan* plan, vk_gather* g, int32_t 
     plan->gather_slot_base = slot_base;
     plan->gather_wait_prev = g && wait_prev != 0;
     return VK_OK;
+}
+
+vk_status vk_decode_plan_gather_wait(const vk_decode_plan* plan, void* workspace, int32_t layer, void* stream) {
+    if (!plan || !plan->gather || !workspace) return fail(VK_INVALID_ARG, "plan without a gather, or no workspace");
+    GatherView gv;
+    if (!gather_view(plan->gather, &gv)) return fail(VK_INVALID_ARG, "gather has peers not imported");
+    if (layer < 0) return fail(VK_INVALID_ARG, "negative layer");
+    const int slot = (plan->gather_slot_base + layer) % gv.slots;
+    DeviceGuard g(plan->device);
+    const uint32_t* epoch = reinterpret_cast<const uint32_t*>(static_cast<const int32_t*>(workspace) + plan->o_hdr);
+    uint32_t* err = reinterpret_cast<uint32_t*>(gv.base[gv.rank] + gv.err_off);
+    plan_gather_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(gv, slot, epoch, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "plan_gather_wait_kernel launch");
 }
 
 int32_t vk_decode_plan_info(const vk_decode_plan* plan, int32_t what) {
@@ -838,7 +867,6 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.tunits = t + plan->o_tu;
     p.ntasks = plan->ntasks;
     p.S = plan->S;
-    p.ndone = plan->ndone;
     p.zunits = t + plan->o_z;
     p.counters = reinterpret_cast<uint32_t*>(ws + plan->counters_off);
     p.part_o = reinterpret_cast<float*>(ws + plan->part_o_off);
@@ -865,7 +893,11 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.U = plan->U;
     p.g = gv;
     p.gslot = gslot;
-    p.gwait_slot = plan->gather_wait_prev ? (gslot + gv.slots - 1) % gv.slots : -1;
+    p.gepoch = reinterpret_cast<const uint32_t*>(t + plan->o_hdr);
+    // run l > 0 signals run l-1's slot; layer 0 follows the previous step's
+    // vk_decode_plan_gather_wait on the stream, which already waited
+    p.gsig_slot = plan->gather && layer > 0 ? (gslot + gv.slots - 1) % gv.slots : -1;
+    p.gwait_slot = plan->gather_wait_prev && layer > 0 ? (gslot + gv.slots - 1) % gv.slots : -1;
     p.out_own = out_own ? 1 : 0;
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;

@@ -1,6 +1,6 @@
-// Receive buffers and flags of the fused head-shard output gather (C ABI),
-// plus the stream wait on one slot.  The peer stores themselves are issued by
-// the planned decode kernel (vk_decode_planned.cu).
+// Receive buffers and flags of the fused head-shard output gather (C ABI).
+// The peer stores, the flag signals and the waits are issued by the planned
+// decode (vk_decode_planned.cu).
 //
 // Each rank allocates one device region with cudaMalloc and shares it with the
 // other processes of the node through CUDA IPC handles; peers map it with
@@ -12,7 +12,8 @@
 
 struct vk_gather {
     int device = 0, rank = 0, world = 0, slots = 0;
-    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, done_off = 0, err_off = 0, total = 0;
+    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, err_off = 0, total = 0;
+    uint32_t epoch = 0;  // steps uploaded with this gather bound (host counter)
     char* own = nullptr;
     char* peer[vk::kMaxGatherRanks] = {};
     bool imported[vk::kMaxGatherRanks] = {};
@@ -30,7 +31,7 @@ bool gather_view(const vk_gather* g, GatherView* v) {
     v->slice_bytes = g->slice_bytes;
     v->slot_bytes = g->slot_bytes;
     v->flags_off = g->flags_off;
-    v->done_off = g->done_off;
+    v->err_off = g->err_off;
     v->rank = g->rank;
     v->world = g->world;
     v->slots = g->slots;
@@ -39,9 +40,7 @@ bool gather_view(const vk_gather* g, GatherView* v) {
 
 int gather_device(const vk_gather* g) { return g ? g->device : -1; }
 
-__global__ void gather_wait_kernel(const GatherView g, int slot, uint32_t* err) {
-    if (threadIdx.x == 0) gather_wait_slot(g, slot, err);
-}
+uint32_t gather_next_epoch(vk_gather* g) { return ++g->epoch; }
 
 }  // namespace vk
 
@@ -65,8 +64,7 @@ vk_status vk_gather_create(int32_t device, int32_t rank, int32_t world, uint64_t
     g->slice_bytes = slice_bytes;
     g->slot_bytes = round256(slice_bytes * static_cast<uint64_t>(world));
     g->flags_off = g->slot_bytes * static_cast<uint64_t>(slots);
-    g->done_off = g->flags_off + round256(static_cast<uint64_t>(slots) * world * sizeof(uint32_t));
-    g->err_off = g->done_off + round256(static_cast<uint64_t>(slots) * sizeof(uint32_t));
+    g->err_off = g->flags_off + round256(static_cast<uint64_t>(slots) * world * sizeof(uint32_t));
     g->total = g->err_off + 256;
     DeviceGuard dg(device);
     cudaError_t e = cudaMalloc(&g->own, g->total);
@@ -139,17 +137,6 @@ void* vk_gather_buffer(const vk_gather* g, int32_t slot) {
     return g->own + static_cast<uint64_t>(slot) * g->slot_bytes;
 }
 
-vk_status vk_gather_wait(vk_gather* g, int32_t slot, void* stream) {
-    if (!g || slot < 0 || slot >= g->slots) return fail(VK_INVALID_ARG, "gather NULL or slot out of range");
-    GatherView v;
-    if (!gather_view(g, &v)) return fail(VK_INVALID_ARG, "gather has peers not imported");
-    DeviceGuard dg(g->device);
-    uint32_t* err = reinterpret_cast<uint32_t*>(g->own + g->err_off);
-    gather_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(v, slot, err);
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? VK_OK : cuda_fail(e, "gather_wait_kernel launch");
-}
-
 vk_status vk_gather_check(vk_gather* g) {
     if (!g) return fail(VK_INVALID_ARG, "gather is NULL");
     DeviceGuard dg(g->device);
@@ -159,7 +146,7 @@ vk_status vk_gather_check(vk_gather* g) {
     if (bits == 0) return VK_OK;
     e = cudaMemset(g->own + g->err_off, 0, sizeof(bits));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(gather error word)");
-    return fail(VK_TIMEOUT, "vk_gather_wait: a rank's slice did not arrive within 1 s");
+    return fail(VK_TIMEOUT, "a gather wait gave up: a rank's slice did not arrive within 1 s");
 }
 
 }  // extern "C"

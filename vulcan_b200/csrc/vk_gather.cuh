@@ -29,11 +29,9 @@ __device__ __forceinline__ uint32_t* gather_flag(const GatherView& g, int on_ran
 }
 
 // One thread: waits until every rank's flag of `slot` in this rank's block has
-// reached this rank's own flag (the count of layers this rank has published in
-// the slot).  Flags only grow (mod 2^32).  False, with VK_ERR_TIMEOUT, after
-// kGatherWaitNs.
-__device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, uint32_t* err) {
-    const uint32_t target = ld_acquire_sys(gather_flag(g, g.rank, slot, g.rank));
+// reached `target` (flags carry step epochs and only grow, mod 2^32).  False,
+// with VK_ERR_TIMEOUT, after kGatherWaitNs.
+__device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, uint32_t target, uint32_t* err) {
     const uint64_t t0 = global_ns();
     for (int r = 0; r < g.world; ++r) {
         const uint32_t* f = gather_flag(g, g.rank, slot, r);
@@ -48,15 +46,12 @@ __device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, 
     return true;
 }
 
-// After every unit of a layer has been stored into all ranks' slices: called by
-// the one thread that counted the last unit.  Raises this rank's flag of
-// `slot` on every rank (own included) to its next value.
-__device__ __forceinline__ void gather_signal(const GatherView& g, int slot) {
-    __threadfence_system();
-    const uint32_t next = *reinterpret_cast<volatile uint32_t*>(gather_flag(g, g.rank, slot, g.rank)) + 1u;
-    for (int r = 0; r < g.world; ++r)
-        if (r != g.rank) st_release_sys(gather_flag(g, r, slot, g.rank), next);
-    st_release_sys(gather_flag(g, g.rank, slot, g.rank), next);
+// One thread, once every store of this rank into `slot` is visible to it (the
+// grid that made them has completed: griddepcontrol.wait or stream order):
+// raises this rank's flag of the slot on every rank to `epoch`.  The release
+// is cumulative, so the peers that acquire the flag see those stores.
+__device__ __forceinline__ void gather_signal(const GatherView& g, int slot, uint32_t epoch) {
+    for (int r = 0; r < g.world; ++r) st_release_sys(gather_flag(g, r, slot, g.rank), epoch);
 }
 
 }  // namespace vk

@@ -88,17 +88,18 @@ int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len);
 
 // Device-side description of a bound output gather (vk_gather), passed by value
 // in kernel parameters.  Allocation of every rank: [slots][world][slice] fp16
-// receive slices, then flags [slots][world] u32 (written only by the rank of
-// the column), then done counters [slots] u32 (local).
+// receive slices, then flags [slots][world] u32 (column r written only by rank
+// r, with step epochs), then an error word (waits outside a pool).
 constexpr int kMaxGatherRanks = 8;
 struct GatherView {
     char* base[kMaxGatherRanks];  // receive allocations of all ranks, own included
-    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, done_off = 0;
+    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, err_off = 0;
     int rank = 0, world = 0, slots = 0;
 };
 // Fills `v` if every peer is imported; false otherwise.
 bool gather_view(const vk_gather* g, GatherView* v);
 int gather_device(const vk_gather* g);
+uint32_t gather_next_epoch(vk_gather* g);
 vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const int32_t* bt, int bt_stride,
                      const int32_t* positions, int B, int T, int Hq, float scale, cudaStream_t st);
 

@@ -301,6 +301,12 @@ class DecodePlan:
               "vk_decode_plan_set_gather")
         self.gather = gather
 
+    def gather_wait(self, layer: int, stream=None) -> None:
+        """Raises this rank's flags for layer's slot (its run precedes on the
+        stream) and makes the stream wait for every rank's slice of it."""
+        check(self._lib.vk_decode_plan_gather_wait(self.handle, _ptr(self.workspace), layer, _stream(stream)),
+              "vk_decode_plan_gather_wait")
+
     @property
     def workers(self) -> int:
         return self.info(0)
@@ -359,7 +365,9 @@ class Gather:
     fp16 output) and ``slots``; the ranks then swap ``export()`` handles over
     any host transport (``exchange`` does it with torch.distributed) and
     ``import_peer`` every other rank's.  ``view(slot, B, Hq_local, D)`` is the
-    rank's receive buffer of a slot as [world, B, Hq_local, D] fp16."""
+    rank's receive buffer of a slot as [world, B, Hq_local, D] fp16.  A step
+    binds it to a plan (``DecodePlan.set_gather``), runs the layers in order and
+    ends with ``DecodePlan.gather_wait(L - 1)``."""
 
     HANDLE_BYTES = 64
 
@@ -403,9 +411,6 @@ class Gather:
             raise ValueError("view larger than the slot")
         arr = _DeviceArray(self.buffer_ptr(slot), (self.world, batch, heads_local, head_dim), "<f2")
         return torch.as_tensor(arr, device=self.device)
-
-    def wait(self, slot: int, stream=None) -> None:
-        check(self._lib.vk_gather_wait(self.handle, slot, _stream(stream)), "vk_gather_wait")
 
     def check(self) -> None:
         check(self._lib.vk_gather_check(self.handle), "vk_gather_check")
