@@ -2,39 +2,48 @@
 //
 // Same contract and arithmetic as the mma.sync prefill in vk_prefill.cu (the
 // causal j <= row rule of cpu_attention, tests/test_attention.cu:66-97, over a
-// cached prefix), head_dim 128.  One CTA per (128-query tile, query head,
-// sequence), one CTA per SM:
+// cached prefix), head_dim 128.  One CTA per (256 query rows, query head,
+// sequence), one CTA per SM, 10 warps.  The 256 rows are two 128-row tiles A
+// and B whose softmax steps alternate, so the tensor core always has the other
+// tile's MMAs to run while one tile's softmax is on the CUDA cores:
 //
-//  * warp 5 allocates 512 TMEM columns (S ping-pong buffers at columns 0 and
-//    128, the O accumulator at 256) and one thread issues every tcgen05.mma:
-//    S_j = Q K_j^T (M=128 queries, N=128 keys, K=128) into S[j%2], then after
-//    softmax_j: O += P_j V_j (M=128, N=128 head dims, K=128 keys).  Completions
-//    are tcgen05.commit arrivals on mbarriers.  Order on the tensor pipe:
-//    S_0, S_1, PV_0, S_2, PV_1, S_3, ... so S_{j+1} runs during softmax_j.
-//  * warp 4 lane 0 streams K and V pages with 2-D TMA boxes of 16 rows x 128 B
-//    (128-byte swizzle) into separate 2-stage K and V rings; a K stage is freed
-//    when its S MMA completes, a V stage when its PV MMA completes.
-//  * warps 0-3: one thread per query row (its TMEM lane).  tcgen05.ld of the S
-//    row, causal mask, row max, P = 2^(s - m) in fp16 written to shared memory in
-//    the UMMA K-major swizzled layout; O is rescaled in TMEM only when the row
-//    max grows by more than 8 (P stays <= 2^8, exact after the final divide).
-//  * All waits are bounded; V rows of keys at or beyond the written length are
-//    zeroed in shared memory before the last PV so stale bytes cannot reach O.
+//  * TMEM (512 columns): S_A at 0, S_B at 128, O_A at 256, O_B at 384.  P of a
+//    tile is written as fp16 pairs over the first 64 columns of its S (after
+//    the softmax has read them) and is the A operand of O += P V straight from
+//    TMEM (tcgen05.mma with A in tensor memory), so P never touches shared
+//    memory.
+//  * warp 9 allocates TMEM and one of its threads issues every tcgen05.mma, in
+//    the order S_A0, S_B0, PV_A0, S_A1, PV_B0, S_B1, PV_A1, S_A2, ... (a tile's
+//    next S is issued after its PV, so P is read before S is rewritten; the
+//    MMAs of one thread execute in issue order).  Completions are
+//    tcgen05.commit arrivals on mbarriers; a K or V stage is released by the
+//    commit after the last MMA that reads it.
+//  * warp 8 lane 0 streams K and V pages with 2-D TMA boxes of 16 rows x 128 B
+//    (128-byte swizzle) into separate 2-stage rings.
+//  * warps 0-3 (tile A) and 4-7 (tile B): one thread per query row (its TMEM
+//    lane).  Per key tile: row max over the S row read from TMEM (masked on the
+//    causal diagonal), P = 2^(s*scale - m) packed to fp16 into TMEM, and O
+//    rescaled in TMEM only when the row max grows by more than 2^8 (P stays
+//    <= 2^8; exact after the final divide).  The scale is folded into one FMA
+//    per element, the max (3-input) and sum run as four independent chains,
+//    and only tiles on the causal diagonal pay for the mask.
+//  * V stages start zeroed, and V rows of keys at or beyond the written length
+//    in the last key tile are zeroed before that tile's PV, so stale bytes
+//    cannot reach O.  All waits are bounded.
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
 
 namespace vk {
 
-constexpr int kTcRows = 128;
+constexpr int kTcRows = 128;                  // rows of one tile; a CTA has two
 constexpr int kTcKeys = 128;
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;
 constexpr int kTcD = 128;
 // shared memory map (bytes from a 1024-aligned base)
-constexpr int kTcQ = 0;                       // [2 halves][128 rows][128 B]
-constexpr int kTcK = 32768;                   // 2 stages x 32 KiB
+constexpr int kTcQ = 0;                       // [2 tiles][2 halves][128 rows][128 B]
+constexpr int kTcK = 65536;                   // 2 stages x 32 KiB
 constexpr int kTcV = kTcK + 2 * 32768;        // 2 stages x 32 KiB
-constexpr int kTcP = kTcV + 2 * 32768;        // [2 halves][128 rows][128 B]
-constexpr int kTcBar = kTcP + 32768;          // mbarriers + TMEM address
+constexpr int kTcBar = kTcV + 2 * 32768;      // mbarriers + TMEM address
 constexpr int kTcSmem = kTcBar + 256 + 1024;
 constexpr uint32_t kTcCols = 512;
 
@@ -64,13 +73,25 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D (TMEM) (+)= A (shared memory) * B (shared memory)
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM, K-major) * B (shared memory)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -112,6 +133,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 
+// 16 consecutive 32-bit columns (here: 32 fp16 of P) of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -126,6 +157,22 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t
 // B K-major (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = 128.
 __device__ __forceinline__ constexpr uint32_t idesc_f16_128x128(uint32_t b_mn) {
     return (1u << 4) | (b_mn << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// 3-input max (one instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Causal mask of 64 scores of a row: key k0 + i is hidden when k0 + i > lim.
+__device__ __forceinline__ void mask_row(float (&v)[2][32], int k0, int lim) {
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (k0 + h2 * 32 + i > lim) v[h2][i] = -INFINITY;
 }
 
 __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, uint32_t* err) {
@@ -144,35 +191,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     uint64_t* k_empty = bars + 2;  // [2]
     uint64_t* v_full = bars + 4;   // [2]
     uint64_t* v_empty = bars + 6;  // [2]
-    uint64_t* s_full = bars + 8;   // [2]
-    uint64_t* p_full = bars + 10;  // softmax -> MMA (count 128)
-    uint64_t* o_full = bars + 11;  // PV done
-    uint64_t* q_full = bars + 12;  // Q in shared memory (count 128)
+    uint64_t* s_full = bars + 8;   // [tile]   S of the tile written
+    uint64_t* p_full = bars + 10;  // [tile]   P written, O rescaled (count 128)
+    uint64_t* o_full = bars + 12;  // [tile]   PV of the tile done
+    uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (count 256)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
-    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
+    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
     const int h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos0 = p.pos[b];
-    const int q0 = qt * kTcRows;
+    const int q0 = qt * 2 * kTcRows;
     if (pos0 < 0 || (pos0 + p.T + P - 1) / P > p.bt_stride) {
         if (threadIdx.x == 0 && qt == 0 && h == 0) atomicOr(p.err, VK_ERR_TABLE_INDEX);
         return;
     }
-    const int kv_len = pos0 + min(p.T, q0 + kTcRows);
-    const int ntiles = (kv_len + kTcKeys - 1) / kTcKeys;
+    // key tiles of each row tile (B may be empty at the end of the chunk)
+    const int rowsA = min(kTcRows, p.T - q0);
+    const int rowsB = max(0, min(kTcRows, p.T - q0 - kTcRows));
+    const int lenA = pos0 + q0 + rowsA;                      // keys tile A attends
+    const int lenB = rowsB > 0 ? pos0 + q0 + kTcRows + rowsB : 0;
+    const int ntA = (lenA + kTcKeys - 1) / kTcKeys;
+    const int ntB = (lenB + kTcKeys - 1) / kTcKeys;
+    const int kv_len = max(lenA, lenB);
+    const int ntiles = max(ntA, ntB);
     const int hkv = h / p.G;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&bars[i]), 1);
-        mbar_init(smem_u32(&s_full[0]), 1);
-        mbar_init(smem_u32(&s_full[1]), 1);
-        mbar_init(smem_u32(p_full), 128);
-        mbar_init(smem_u32(o_full), 1);
-        mbar_init(smem_u32(q_full), 128);
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(smem_u32(&s_full[t]), 1);
+            mbar_init(smem_u32(&p_full[t]), 128);
+            mbar_init(smem_u32(&o_full[t]), 1);
+        }
+        mbar_init(smem_u32(q_full), 256);
         mbar_fence_init();
     }
-    if (warp == 5) {
+    // zero both V stages: rows a last tile does not load keep finite values
+    for (int i = threadIdx.x; i < 2 * 32768 / 16; i += kTcThreads)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(sbase + kTcV + i * 16), "r"(0u) : "memory");
+    fence_async_smem();
+    if (warp == 9) {
         tmem_alloc(smem_u32(tmem_slot), kTcCols);
         tmem_relinquish();
     }
@@ -181,7 +240,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             prefetch_tmap(&tmap16);
@@ -219,51 +278,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                 }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t id_s = idesc_f16_128x128(0), id_pv = idesc_f16_128x128(1);
             bool ok = mbar_wait(smem_u32(q_full), 0, p.err);
             tc_fence_after();
-            auto issue_s = [&](int j) {
+            const int nt[2] = {ntA, ntB};
+            int k_waited = -1;  // highest key tile whose K stage has been waited for
+            auto issue_s = [&](int t, int j) {
                 const int st = j & 1;
-                ok = ok && mbar_wait(smem_u32(&k_full[st]), (j >> 1) & 1, p.err);
+                if (j > k_waited) {
+                    ok = ok && mbar_wait(smem_u32(&k_full[st]), (j >> 1) & 1, p.err);
+                    k_waited = j;
+                }
                 if (!ok) return;
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kTcD / 16; ++ks) {
                     const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-                    umma_f16(tmem + st * 128, umma_desc_sw128(sbase + kTcQ + off, 16, 1024),
-                             umma_desc_sw128(sbase + kTcK + st * 32768 + off, 16, 1024), id_s, ks > 0);
+                    umma_ss(tmem + t * 128, umma_desc_sw128(sbase + kTcQ + t * 32768 + off, 16, 1024),
+                            umma_desc_sw128(sbase + kTcK + st * 32768 + off, 16, 1024), id_s, ks > 0);
                 }
-                umma_commit(smem_u32(&s_full[st]));
-                umma_commit(smem_u32(&k_empty[st]));
+                umma_commit(smem_u32(&s_full[t]));
+                // the last S that reads this K stage releases it
+                if (t == 1 || j >= ntB) umma_commit(smem_u32(&k_empty[st]));
             };
-            if (ok) issue_s(0);
-            if (ok && ntiles > 1) issue_s(1);
-            for (int j = 0; j < ntiles && ok; ++j) {
+            auto issue_pv = [&](int t, int j) {
                 const int st = j & 1;
-                ok = mbar_wait(smem_u32(p_full), j & 1, p.err) && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
-                if (!ok) break;
+                ok = ok && mbar_wait(smem_u32(&p_full[t]), j & 1, p.err);
+                if (t == 0 || j >= ntA) ok = ok && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
+                if (!ok) return;
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-                    const uint64_t a = umma_desc_sw128(sbase + kTcP + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
                     const uint64_t bv = umma_desc_sw128(sbase + kTcV + st * 32768 + ks * 2048, 16384, 1024);
-                    umma_f16(tmem + 256, a, bv, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, bv, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
                 }
-                umma_commit(smem_u32(o_full));
-                umma_commit(smem_u32(&v_empty[st]));
-                if (j + 2 < ntiles) issue_s(j + 2);
+                umma_commit(smem_u32(&o_full[t]));
+                if (t == 1 || j >= ntB) umma_commit(smem_u32(&v_empty[st]));
+            };
+            if (ntA > 0) issue_s(0, 0);
+            if (ntB > 0) issue_s(1, 0);
+            for (int j = 0; j < ntiles && ok; ++j) {
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    if (j < nt[t]) {
+                        issue_pv(t, j);
+                        if (j + 1 < nt[t]) issue_s(t, j + 1);
+                    }
+                }
             }
         }
     } else {
         // ------------------------------------------------------------ softmax (one query row per thread)
-        const int r = threadIdx.x;  // 0..127 = TMEM lane
-        const int qrow = q0 + r;
+        const int t = warp >> 2;              // row tile
+        const int r = threadIdx.x & 127;      // row in the tile = TMEM lane
+        const int qrow = q0 + t * kTcRows + r;
         const bool valid_row = qrow < p.T;
         const int qpos = pos0 + qrow;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const int ntt = t ? ntB : ntA;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+        const uint32_t s_col = t * 128, o_col = 256 + t * 128;
         // Q row -> shared memory (K-major, 128-byte swizzle)
         {
             const uint4* src = reinterpret_cast<const uint4*>(
@@ -271,7 +347,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 uint4 v = valid_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-                const uint32_t addr = sbase + kTcQ + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                const uint32_t addr =
+                    sbase + kTcQ + t * 32768 + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
                 asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
                              "r"(v.w)
                              : "memory");
@@ -279,96 +356,108 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
             fence_async_smem();
             mbar_arrive(smem_u32(q_full));
         }
-        float m_ref = -INFINITY, l = 0.f;
+        const float sc = p.scale_log2;
+        float m_ref = -INFINITY, l = 0.f;  // m_ref in the scaled (log2) domain
         bool alive = true;
-        for (int j = 0; j < ntiles && alive; ++j) {
-            const int st = j & 1;
-            if (!wait_warp(smem_u32(&s_full[st]), (j >> 1) & 1, p.err)) { alive = false; break; }
+        for (int j = 0; j < ntt && alive; ++j) {
+            if (!wait_warp(smem_u32(&s_full[t]), j & 1, p.err)) { alive = false; break; }
             tc_fence_after();
-            float s[kTcKeys];
-#pragma unroll
-            for (int c = 0; c < kTcKeys / 32; ++c) {
-                float v[32];
-                tmem_ld32(lane_base + st * 128 + c * 32, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
-            }
-            tmem_wait_ld();
             const int key0 = j * kTcKeys;
-            const bool need_mask = key0 + kTcKeys - 1 > pos0 + q0;  // any key past the tile's first row
-            float mx = -INFINITY;
+            // keys past the tile's first row need the causal mask
+            const bool need_mask = key0 + kTcKeys - 1 > pos0 + q0 + t * kTcRows;
+            const int lim = qpos - key0;  // key c is visible iff c <= lim
+            // pass 1: row max of the raw scores (scale > 0 commutes with max);
+            // masked keys read as -inf, so their P below is 2^-inf = 0
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < kTcKeys; ++c) {
-                float v = s[c] * p.scale_log2;
-                if (need_mask && key0 + c > qpos) v = -INFINITY;
-                s[c] = v;
-                mx = fmaxf(mx, v);
+            for (int c2 = 0; c2 < kTcKeys / 64; ++c2) {
+                float v[2][32];
+                tmem_ld32(lane_base + s_col + c2 * 64, v[0]);
+                tmem_ld32(lane_base + s_col + c2 * 64 + 32, v[1]);
+                tmem_wait_ld();
+                if (need_mask) mask_row(v, c2 * 64, lim);
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        mx4[0] = max3f(mx4[0], v[h2][i], v[h2][i + 1]);
+                        mx4[1] = max3f(mx4[1], v[h2][i + 2], v[h2][i + 3]);
+                        mx4[2] = max3f(mx4[2], v[h2][i + 4], v[h2][i + 5]);
+                        mx4[3] = max3f(mx4[3], v[h2][i + 6], v[h2][i + 7]);
+                    }
             }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
             float alpha = 1.f;
             if (mx > m_ref + 8.f || m_ref == -INFINITY) {  // lazy rescale
                 const float m_new = fmaxf(m_ref, mx);
                 alpha = ex2(m_ref - m_new);
                 m_ref = m_new;
             }
-            float rowsum = 0.f;
-            uint32_t pk[kTcKeys / 2];
+            // pass 2: P = 2^(s*sc - m_ref), packed to fp16 over the first 64
+            // columns of S (column 16c+i holds keys 32c+2i, 32c+2i+1)
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+            const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
 #pragma unroll
-            for (int c = 0; c < kTcKeys; c += 2) {
-                const float a0 = ex2(s[c] - m_ref), a1 = ex2(s[c + 1] - m_ref);
-                rowsum += a0 + a1;
-                pk[c >> 1] = pack_half2(a0, a1);
-            }
-            l = l * alpha + rowsum;
-            // PV_{j-1} must be done before P is overwritten and O rescaled
-            if (j > 0) {
-                if (!wait_warp(smem_u32(o_full), (j - 1) & 1, p.err)) { alive = false; break; }
-                tc_fence_after();
-            }
+            for (int c2 = 0; c2 < kTcKeys / 64; ++c2) {
+                float v[2][32];
+                tmem_ld32(lane_base + s_col + c2 * 64, v[0]);
+                tmem_ld32(lane_base + s_col + c2 * 64 + 32, v[1]);
+                tmem_wait_ld();
+                if (need_mask) mask_row(v, c2 * 64, lim);
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
-                const uint32_t addr = sbase + kTcP + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]),
-                             "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
-                             : "memory");
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float a0 = ex2(fmaf(v[h2][i], sc, mneg));
+                        const float a1 = ex2(fmaf(v[h2][i + 1], sc, mneg));
+                        sum4[(i >> 1) & 3] += a0 + a1;
+                        pk[i >> 1] = pack_half2(a0, a1);
+                    }
+                    tmem_st16(lane_base + s_col + (2 * c2 + h2) * 16, pk);
+                }
             }
-            // tcgen05.ld/st are warp-collective: rescale if any row of the warp needs it
+            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            // tcgen05.ld/st are warp-collective: rescale O if any row of the warp
+            // needs it (PV of the previous tile completed before this S was written)
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
                 for (int c = 0; c < kTcD / 32; ++c) {
                     float v[32];
-                    tmem_ld32(lane_base + 256 + c * 32, v);
+                    tmem_ld32(lane_base + o_col + c * 32, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] *= alpha;
-                    tmem_st32(lane_base + 256 + c * 32, v);
+                    tmem_st32(lane_base + o_col + c * 32, v);
                 }
-                tmem_wait_st();
             }
+            tmem_wait_st();
             if (j == ntiles - 1 && key0 + kTcKeys > kv_len) {
-                // zero V rows of keys at or beyond the written length (last tile only)
-                if (!wait_warp(smem_u32(&v_full[st]), (j >> 1) & 1, p.err)) { alive = false; break; }
+                // the CTA's last key tile: zero V rows of keys at or beyond the
+                // written length (both tiles may do it; same zeros)
+                if (!wait_warp(smem_u32(&v_full[j & 1]), (j >> 1) & 1, p.err)) { alive = false; break; }
                 if (key0 + r >= kv_len) {
 #pragma unroll
                     for (int hb = 0; hb < 2; ++hb)
 #pragma unroll
                         for (int c = 0; c < 8; ++c) {
-                            const uint32_t addr = sbase + kTcV + st * 32768 + hb * 16384 + r * 128 + (c << 4);
+                            const uint32_t addr = sbase + kTcV + (j & 1) * 32768 + hb * 16384 + r * 128 + (c << 4);
                             asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
                         }
                 }
+                fence_async_smem();
             }
-            fence_async_smem();
             tc_fence_before();
-            mbar_arrive(smem_u32(p_full));
+            mbar_arrive(smem_u32(&p_full[t]));
         }
-        if (alive && wait_warp(smem_u32(o_full), (ntiles - 1) & 1, p.err)) {
+        if (alive && ntt > 0 && wait_warp(smem_u32(&o_full[t]), (ntt - 1) & 1, p.err)) {
             tc_fence_after();
             const float inv = 1.f / l;
             __half* dst = p.out + ((static_cast<int64_t>(b) * p.T + (valid_row ? qrow : 0)) * p.Hq + h) * kTcD;
 #pragma unroll
             for (int c = 0; c < kTcD / 32; ++c) {
                 float v[32];
-                tmem_ld32(lane_base + 256 + c * 32, v);
+                tmem_ld32(lane_base + o_col + c * 32, v);
                 tmem_wait_ld();
                 if (valid_row) {
 #pragma unroll
@@ -386,7 +475,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
         tc_fence_before();
     }
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem, kTcCols);
     }
@@ -421,7 +510,7 @@ vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const i
     p.G = Hq / p.Hkv;
     p.layer = layer;
     p.num_pages = pool->num_pages;
-    p.q_tiles = (T + kTcRows - 1) / kTcRows;
+    p.q_tiles = (T + 2 * kTcRows - 1) / (2 * kTcRows);
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(kTcD));
     p.scale_log2 = sc * 1.4426950408889634f;
     return launch_prefill_tc(pool, p, B, st);
