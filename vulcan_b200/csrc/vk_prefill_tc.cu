@@ -26,8 +26,7 @@
 //    rescaled in TMEM only when the row max grows by more than 2^8 (P stays
 //    <= 2^8; exact after the final divide).  The scale is folded into one FMA
 //    per element, the max (3-input) and sum run as four independent chains,
-//    only tiles on the causal diagonal pay for the mask, and a quarter of the
-//    exponentials run as a polynomial on the FMA pipe beside the SFU.
+//    and only tiles on the causal diagonal pay for the mask.
 //  * V stages start zeroed, and V rows of keys at or beyond the written length
 //    in the last key tile are zeroed before that tile's PV, so stale bytes
 //    cannot reach O.  All waits are bounded.
@@ -158,23 +157,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t
 // B K-major (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = 128.
 __device__ __forceinline__ constexpr uint32_t idesc_f16_128x128(uint32_t b_mn) {
     return (1u << 4) | (b_mn << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-}
-
-// 2^x on the FMA pipe, to share the exponentials of P between the SFU and the
-// FMA units.  Range reduction x = n + f with n = round(x) (adding 1.5 * 2^23
-// leaves n in the low mantissa bits) and f in [-1/2, 1/2]; 2^f by a degree-3
-// polynomial whose coefficients are a relative-error minimax fit (Lawson's
-// iteratively reweighted least squares) on that interval, max relative error
-// 7.5e-5, below half an fp16 ulp; 2^n added to the exponent field.  x is
-// clamped to >= -126 (2^-126 rounds to fp16 zero), so -inf gives ~1e-38.
-__device__ __forceinline__ float ex2_poly(float x) {
-    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-    x = fmaxf(x, -126.0f);
-    const float t = __fadd_rn(x, kRound);
-    const float f = __fsub_rn(x, __fsub_rn(t, kRound));
-    const float p = fmaf(fmaf(fmaf(0.05517132207751274f, f, 0.24261054396629333f), f, 0.6932609677314758f), f,
-                         0.9999281167984009f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // 3-input max (one instruction on sm_100)
@@ -427,10 +409,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                     uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        // one exponential in four on the FMA pipe
                         const float a0 = ex2(fmaf(v[h2][i], sc, mneg));
-                        const float x1 = fmaf(v[h2][i + 1], sc, mneg);
-                        const float a1 = (i & 2) ? ex2_poly(x1) : ex2(x1);
+                        const float a1 = ex2(fmaf(v[h2][i + 1], sc, mneg));
                         sum4[(i >> 1) & 3] += a0 + a1;
                         pk[i >> 1] = pack_half2(a0, a1);
                     }
