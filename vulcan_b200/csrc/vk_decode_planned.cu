@@ -138,16 +138,26 @@ __device__ __forceinline__ void publish_unit(const PlanParams& p, int u, int lan
     publish_heads<D>(p, u, 0, p.G, lane);
 }
 
-// Fused gather, after griddepcontrol.wait: warp 0 raises this rank's flags for
-// the preceding run's slot; then (strict order) every warp waits until all
-// ranks' slices of the previous slot have arrived.
+// Fused gather, after griddepcontrol.wait.  Strict order (a wait slot): warp 0
+// raises this rank's flags for the preceding run's slot, then every warp waits
+// until all ranks' slices of that slot have arrived.  Otherwise the flags are
+// raised at the end (gather_epilogue), off the critical path.
 __device__ __forceinline__ void gather_prologue(const PlanParams& p, int w, int lane) {
-    if (p.g.world == 0) return;
+    if (p.g.world == 0 || p.gwait_slot < 0) return;
     const uint32_t epoch = *p.gepoch;
     if (w == 0 && lane == 0 && p.gsig_slot >= 0) gather_signal(p.g, p.gsig_slot, epoch);
-    if (p.gwait_slot < 0) return;
     if (lane == 0) gather_wait_slot(p.g, p.gwait_slot, epoch, p.err);
     __syncwarp();
+}
+
+// Fused gather without the strict order: the first warp to finish its work
+// raises this rank's flags for the preceding run's slot (each slot records the
+// epoch it was last raised with, so exactly one warp does it).
+__device__ __forceinline__ void gather_epilogue(const PlanParams& p, int lane) {
+    if (p.g.world == 0 || p.gwait_slot >= 0 || p.gsig_slot < 0 || lane != 0) return;
+    const uint32_t epoch = *p.gepoch;
+    unsigned int* sig = reinterpret_cast<unsigned int*>(p.g.base[p.g.rank] + p.g.sig_off) + p.gsig_slot;
+    if (static_cast<int32_t>(atomicMax(sig, epoch) - epoch) < 0) gather_signal(p.g, p.gsig_slot, epoch);
 }
 
 // Iterator over (unit, page-in-unit) along the concatenated page list.
@@ -352,6 +362,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             publish_unit<D>(p, p.zunits[i], lane);
         }
         run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
+        gather_epilogue(p, lane);
         return;
     }
 
@@ -552,6 +563,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
         }
     }
     run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
+    gather_epilogue(p, lane);
 }
 
 // Signals this rank's stores of `slot` (the preceding run on the stream has

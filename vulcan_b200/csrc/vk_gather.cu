@@ -12,7 +12,7 @@
 
 struct vk_gather {
     int device = 0, rank = 0, world = 0, slots = 0;
-    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, err_off = 0, total = 0;
+    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, sig_off = 0, err_off = 0, total = 0;
     uint32_t epoch = 0;  // steps uploaded with this gather bound (host counter)
     char* own = nullptr;
     char* peer[vk::kMaxGatherRanks] = {};
@@ -31,6 +31,7 @@ bool gather_view(const vk_gather* g, GatherView* v) {
     v->slice_bytes = g->slice_bytes;
     v->slot_bytes = g->slot_bytes;
     v->flags_off = g->flags_off;
+    v->sig_off = g->sig_off;
     v->err_off = g->err_off;
     v->rank = g->rank;
     v->world = g->world;
@@ -64,7 +65,8 @@ vk_status vk_gather_create(int32_t device, int32_t rank, int32_t world, uint64_t
     g->slice_bytes = slice_bytes;
     g->slot_bytes = round256(slice_bytes * static_cast<uint64_t>(world));
     g->flags_off = g->slot_bytes * static_cast<uint64_t>(slots);
-    g->err_off = g->flags_off + round256(static_cast<uint64_t>(slots) * world * sizeof(uint32_t));
+    g->sig_off = g->flags_off + round256(static_cast<uint64_t>(slots) * world * sizeof(uint32_t));
+    g->err_off = g->sig_off + round256(static_cast<uint64_t>(slots) * sizeof(uint32_t));
     g->total = g->err_off + 256;
     DeviceGuard dg(device);
     cudaError_t e = cudaMalloc(&g->own, g->total);

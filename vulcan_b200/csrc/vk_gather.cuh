@@ -48,10 +48,14 @@ __device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, 
 
 // One thread, once every store of this rank into `slot` is visible to it (the
 // grid that made them has completed: griddepcontrol.wait or stream order):
-// raises this rank's flag of the slot on every rank to `epoch`.  The release
-// is cumulative, so the peers that acquire the flag see those stores.
+// raises this rank's flag of the slot on every rank to `epoch`.  One
+// system-scope fence, then relaxed stores: a release pattern, so the peers
+// that acquire a flag see those stores.
 __device__ __forceinline__ void gather_signal(const GatherView& g, int slot, uint32_t epoch) {
-    for (int r = 0; r < g.world; ++r) st_release_sys(gather_flag(g, r, slot, g.rank), epoch);
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < g.world; ++r)
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(gather_flag(g, r, slot, g.rank)), "r"(epoch)
+                     : "memory");
 }
 
 }  // namespace vk

@@ -89,11 +89,12 @@ int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len);
 // Device-side description of a bound output gather (vk_gather), passed by value
 // in kernel parameters.  Allocation of every rank: [slots][world][slice] fp16
 // receive slices, then flags [slots][world] u32 (column r written only by rank
-// r, with step epochs), then an error word (waits outside a pool).
+// r, with step epochs), then [slots] u32 epochs already signalled by this rank
+// (local), then an error word (waits outside a pool).
 constexpr int kMaxGatherRanks = 8;
 struct GatherView {
     char* base[kMaxGatherRanks];  // receive allocations of all ranks, own included
-    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, err_off = 0;
+    uint64_t slice_bytes = 0, slot_bytes = 0, flags_off = 0, sig_off = 0, err_off = 0;
     int rank = 0, world = 0, slots = 0;
 };
 // Fills `v` if every peer is imported; false otherwise.
