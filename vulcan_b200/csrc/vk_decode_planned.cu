@@ -176,65 +176,24 @@ struct PageIt {
 
 
 // One merge task: heads [h0, h0 + hs) of unit u from its np piece partials,
-// out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), written as fp16.  IT =
-// float4 items per lane (items f = lane + 32 i, i < IT, of the task's
-// [hs, D] block).  The lse pass reads up to 64 pieces per round (piece k in
-// lane k % 32); the o pass issues the loads of KB pieces together.
+// out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), written as fp16, in one
+// streaming pass with a running max.  IT = float4 items per lane (items
+// f = lane + 32 i, i < IT, of the task's [hs, D] block); the loads of KB
+// pieces (partials and their lse) are issued together.
 template <int D, int NT, int IT>
 __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, int hs, int np, int lane) {
-    constexpr int GMAX = 8 * NT;
-    constexpr int KMAX = 2;
-    constexpr int KB = 16 / IT;
+    constexpr int KB = IT == 1 ? 32 : 16 / IT;
     const int base = p.uslot[u];
     const int nf = hs * D / 4;
-    float m[GMAX], den[GMAX];
-#pragma unroll
-    for (int hh = 0; hh < GMAX; ++hh) {
-        m[hh] = -INFINITY;
-        den[hh] = 0.f;
-    }
-    for (int k0 = 0; k0 < np; k0 += 32 * KMAX) {
-        float lv[GMAX][KMAX];
-#pragma unroll
-        for (int hh = 0; hh < GMAX; ++hh)
-#pragma unroll
-            for (int r = 0; r < KMAX; ++r) {
-                const int k = k0 + r * 32 + lane;
-                lv[hh][r] = (hh < hs && k < np) ? __ldcg(p.part_lse + static_cast<int64_t>(base + k) * p.G + h0 + hh)
-                                                : -INFINITY;
-            }
-#pragma unroll
-        for (int hh = 0; hh < GMAX; ++hh) {
-            if (hh < hs) {
-                float mx = fmaxf(lv[hh][0], lv[hh][1]);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                const float mn = fmaxf(m[hh], mx);
-                float e = 0.f;
-#pragma unroll
-                for (int r = 0; r < KMAX; ++r) e += ex2(lv[hh][r] - mn);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
-                den[hh] = den[hh] * ex2(m[hh] - mn) + e;
-                m[hh] = mn;
-            }
-        }
-    }
-    float mi[IT], di[IT];
+    float m[IT], den[IT];
     int hi[IT];
     float4 acc[IT];
 #pragma unroll
     for (int i = 0; i < IT; ++i) {
         const int f = lane + 32 * i;
         hi[i] = f < nf ? (f * 4) / D : 0;
-        mi[i] = m[0];
-        di[i] = den[0];
-#pragma unroll
-        for (int q = 1; q < GMAX; ++q)
-            if (q == hi[i]) {
-                mi[i] = m[q];
-                di[i] = den[q];
-            }
+        m[i] = -INFINITY;
+        den[i] = 0.f;
         acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const float4* os = reinterpret_cast<const float4*>(p.part_o);
@@ -254,27 +213,40 @@ __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, i
                 lw[b][i] = live ? __ldcg(p.part_lse + k * p.G + h0 + hi[i]) : -INFINITY;
             }
 #pragma unroll
-        for (int b = 0; b < KB; ++b)
+        for (int i = 0; i < IT; ++i) {
+            float mb = m[i];
 #pragma unroll
-            for (int i = 0; i < IT; ++i) {
-                const float wgt = ex2(lw[b][i] - mi[i]);
+            for (int b = 0; b < KB; ++b) mb = fmaxf(mb, lw[b][i]);
+            if (mb == -INFINITY) continue;  // no piece for this item yet
+            const float a = ex2(m[i] - mb);  // 0 while m is -inf
+            den[i] *= a;
+            acc[i].x *= a;
+            acc[i].y *= a;
+            acc[i].z *= a;
+            acc[i].w *= a;
+#pragma unroll
+            for (int b = 0; b < KB; ++b) {
+                const float wgt = ex2(lw[b][i] - mb);
+                den[i] += wgt;
                 acc[i].x += wgt * ov[b][i].x;
                 acc[i].y += wgt * ov[b][i].y;
                 acc[i].z += wgt * ov[b][i].z;
                 acc[i].w += wgt * ov[b][i].w;
             }
+            m[i] = mb;
+        }
     }
     const int64_t head0 = static_cast<int64_t>(u / p.Hkv) * p.Hq + (u % p.Hkv) * p.G + h0;
 #pragma unroll
     for (int i = 0; i < IT; ++i) {
         const int f = lane + 32 * i;
         if (f < nf) {
-            const float inv = 1.f / di[i];
+            const float inv = 1.f / den[i];
             const __half2 lo = __floats2half2_rn(acc[i].x * inv, acc[i].y * inv);
-            const __half2 hi = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
+            const __half2 hi2 = __floats2half2_rn(acc[i].z * inv, acc[i].w * inv);
             uint2 v;
             v.x = *reinterpret_cast<const uint32_t*>(&lo);
-            v.y = *reinterpret_cast<const uint32_t*>(&hi);
+            v.y = *reinterpret_cast<const uint32_t*>(&hi2);
             *reinterpret_cast<uint2*>(p.out + head0 * D + f * 4) = v;
             // fused gather: the same 8 bytes into every rank's receive slice
             const uint64_t off = static_cast<uint64_t>(p.gslot) * p.g.slot_bytes +
