@@ -20,9 +20,12 @@
 //    the new rows.
 //  * Merge fused: a unit covered by one worker writes its fp16 output directly;
 //    otherwise each piece writes its normalised partial and log2-sum-exp and
-//    counts itself on the unit.  Merges are tasks of (unit, group of query
-//    heads) dealt to all warps of the grid by the plan; a warp runs its tasks
-//    after its own page range, each once the unit's pieces are all counted
+//    counts itself on the unit.  When workers have long ranges (>= 64 pages),
+//    a unit of at most 8 pieces is merged by its last piece at once.  Other
+//    units (and all of them for small per-GPU shares, where every piece ends
+//    at the same time) are merged by tasks of (unit, group of query heads)
+//    dealt to all warps of the grid by the plan; a warp runs its tasks after
+//    its own page range, each once the unit's pieces are all counted
 //    (bounded wait).  No warp merges in the middle of its range, and the merge
 //    of a unit split into many pieces is spread over up to G warps.
 //  * Gather fused (optional, head-sharded multi-GPU): each finished unit output
@@ -41,6 +44,8 @@ namespace vk {
 constexpr int kPlanWarps = 2;      // worker warps per CTA
 constexpr int kPlanStages = 4;     // TMA stages per worker (8 KiB each at D=128)
 constexpr int kMinPagesPerWorker = 8;
+constexpr int kLastMergeMax = 8;   // large shares: units of up to this many pieces merge in their last piece
+constexpr int kLastMergeMinPages = 64;  // ... when workers have at least this many pages
 
 struct PlanParams {
     const int32_t* wb;     // [W+1] first global page of each worker
@@ -65,6 +70,7 @@ struct PlanParams {
     uint64_t seg_bytes, layer_off, head_bytes;
     int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z, U;
     int ntasks, S;   // merge tasks, tasks (head groups) per split unit
+    int lmm;         // units of up to lmm pieces merge in their last piece (others: tasks)
     float scale_log2;
     // fused output gather (g.world == 0: none)
     GatherView g;
@@ -182,7 +188,7 @@ struct PageIt {
 // pieces (partials and their lse) are issued together.
 template <int D, int NT, int IT>
 __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, int hs, int np, int lane) {
-    constexpr int KB = IT == 1 ? 32 : 16 / IT;
+    constexpr int KB = IT == 1 ? 32 : (IT >= 16 ? 1 : 16 / IT);
     const int base = p.uslot[u];
     const int nf = hs * D / 4;
     float m[IT], den[IT];
@@ -522,7 +528,23 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                     }
                 }
                 __syncwarp();  // every lane's partial stores precede lane 0's release
-                if (lane == 0) atom_add_release_gpu(&p.counters[u], 1u);
+                if (npieces > p.lmm) {
+                    if (lane == 0) atom_add_release_gpu(&p.counters[u], 1u);
+                } else {
+                    // few pieces: the last to finish merges the unit at once
+                    unsigned int prev = 0;
+                    if (lane == 0) prev = atom_add_acq_rel_gpu(&p.counters[u], 1u);
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    if (prev == static_cast<unsigned int>(npieces - 1)) {
+                        __syncwarp();  // lane 0's acquire precedes every lane's loads
+                        // head groups of at most 8 float4 items per lane
+                        constexpr int HG = 1024 / D;
+                        for (int hg = 0; hg < p.G; hg += HG)
+                            merge_task<D, NT, (HG * D / 128 < NT * 8 * D / 128 ? HG * D / 128 : NT * 8 * D / 128)>(
+                                p, u, hg, min(HG, p.G - hg), npieces, lane);
+                        if (lane == 0) p.counters[u] = 0u;
+                    }
+                }
             }
             if (j + 1 < n) {
                 cu.next(p.uoff);
@@ -583,7 +605,7 @@ struct vk_decode_plan {
     int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
     mutable std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
-    int ntasks = 0, S = 1;
+    int ntasks = 0, S = 1, lmm = 1;
     size_t o_hdr = 0;  // [0]: step epoch written at upload (fused gather)
     size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
     bool early_start = false;
@@ -654,6 +676,10 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     int64_t W = T > 0 ? std::min<int64_t>(cap, (T + kMinPagesPerWorker - 1) / kMinPagesPerWorker) : 0;
     W = std::max<int64_t>(W, T > 0 ? 1 : 0);
     pl->W = static_cast<int>(W);
+    // with long worker ranges a unit's few pieces end at different times: the
+    // last merges at once; with short ranges (small per-GPU shares) all pieces
+    // end together and the merges are spread over the grid as tasks
+    pl->lmm = (W > 0 && T / W >= kLastMergeMinPages) ? kLastMergeMax : 1;
     const int zero_ctas = (pl->Z + kPlanWarps - 1) / kPlanWarps;
     pl->grid = static_cast<int>(std::max<int64_t>((W + kPlanWarps - 1) / kPlanWarps, std::min<int64_t>(zero_ctas, cap / kPlanWarps)));
     if (pl->grid == 0 && pl->Z > 0) pl->grid = 1;
@@ -687,7 +713,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         if (unp[u] > 1) {
             uslot[u] = slots;
             slots += unp[u];
-            tunits.push_back(u);
+            if (unp[u] > pl->lmm) tunits.push_back(u);  // merged by dealt tasks
         }
     }
     pl->slots = slots;
@@ -851,6 +877,7 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.tunits = t + plan->o_tu;
     p.ntasks = plan->ntasks;
     p.S = plan->S;
+    p.lmm = plan->lmm;
     p.zunits = t + plan->o_z;
     p.counters = reinterpret_cast<uint32_t*>(ws + plan->counters_off);
     p.part_o = reinterpret_cast<float*>(ws + plan->part_o_off);
