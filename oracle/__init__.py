@@ -56,6 +56,8 @@ def lib():
         L.or_copy_pages.restype = _c_int
         L.or_remap_block_tables.argtypes = [_i32p, ctypes.c_int64, _i32p, _c_int]
         L.or_remap_block_tables.restype = None
+        L.or_rope.argtypes = [_f32p, _f32p, _c_int, _c_int, ctypes.c_float]
+        L.or_rope.restype = None
         _LIB = L
     return _LIB
 
@@ -72,6 +74,10 @@ def ref_lib():
         R.ref_random_floats.restype = None
         R.ref_cpu_attention.argtypes = [_f32p, _f32p, _f32p, _f32p] + [_c_int] * 4
         R.ref_cpu_attention.restype = None
+        R.ref_kernels_random_floats.argtypes = [_c_int, ctypes.c_float, ctypes.c_float, _c_int, _f32p]
+        R.ref_kernels_random_floats.restype = None
+        R.ref_cpu_rope.argtypes = [_f32p, _c_int, _c_int, ctypes.c_float, _f32p]
+        R.ref_cpu_rope.restype = None
         _REF = R
     return _REF
 
@@ -191,4 +197,38 @@ def ref_random_floats(n, lo, hi, seed):
         raise RuntimeError("oracle/_ref not built")
     out = np.zeros(n, np.float32)
     R.ref_random_floats(n, lo, hi, seed, out)
+    return out
+
+
+def rope(x, positions, theta_base=10000.0):
+    """cpu_rope (tests/test_kernels.cu:697-716) over the last axis of x (fp32),
+    row r of x.reshape(-1, D) at positions.reshape(-1)[r // rows_per_pos]:
+    positions has one entry per leading index of x.shape[:-1] prefix it
+    broadcasts against (same shape as x.shape[:k] for some k)."""
+    x = np.ascontiguousarray(x, np.float32)
+    D = x.shape[-1]
+    pos = np.asarray(positions, np.int32)
+    rows = x.reshape(-1, D)
+    per = rows.shape[0] // max(1, pos.size)
+    out = np.empty_like(rows)
+    L = lib()
+    for r in range(rows.shape[0]):
+        L.or_rope(np.ascontiguousarray(rows[r]), out[r], D, int(pos.reshape(-1)[r // per]), float(theta_base))
+    return out.reshape(x.shape)
+
+
+def ref_rope(x, pos, theta_base=10000.0):
+    """The reference's own cpu_rope on one vector (needs oracle/_ref)."""
+    R = ref_lib()
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    R.ref_cpu_rope(x, x.size, int(pos), float(theta_base), out)
+    return out
+
+
+def ref_kernels_random_floats(n, lo, hi, seed):
+    """random_floats of the reference's kernel tests (tests/test_kernels.cu:30-37)."""
+    R = ref_lib()
+    out = np.empty(n, np.float32)
+    R.ref_kernels_random_floats(n, lo, hi, seed, out)
     return out

@@ -11,6 +11,8 @@
  *   - KVCache::append         src/kv_cache.cpp:84-128          (row scatter)
  *   - GQA head mapping        src/transformer.cpp:173-189      (q_head = kv*G + rep)
  *   - MemoryManager pages     cuda/memory.cu:73-191            (byte pages, swap)
+ *   - cpu_rope                tests/test_kernels.cu:697-716    (rotary embedding,
+ *                             applied to Q and K_new at src/transformer.cpp:114-128)
  *
  * Floating point follows cpu_attention exactly: fp32 accumulation in the same
  * loop order, -FLT_MAX fill, max-subtracted expf, divide by the sum, then the
@@ -338,4 +340,22 @@ int or_decode_paged_f64(const uint16_t* pool, int L, int Hkv, int D, int P, int 
         free(s);
     }
     return 0;
+}
+
+/* RoPE of one head_dim vector at position pos, restating cpu_rope
+ * (tests/test_kernels.cu:697-716) step for step: pair i = (2i, 2i+1),
+ * freq = 1 / theta_base^(2i/head_dim), angle = pos * freq,
+ * (x0 cos - x1 sin, x0 sin + x1 cos).  `in` and `out` may alias. */
+void or_rope(const float* in, float* out, int head_dim, int pos, float theta_base) {
+    const int half = head_dim / 2;
+    for (int i = 0; i < half; ++i) {
+        const float freq = 1.0f / powf(theta_base, 2.0f * (float)i / (float)head_dim);
+        const float theta = (float)pos * freq;
+        const float cos_t = cosf(theta);
+        const float sin_t = sinf(theta);
+        const float x0 = in[2 * i];
+        const float x1 = in[2 * i + 1];
+        out[2 * i] = x0 * cos_t - x1 * sin_t;
+        out[2 * i + 1] = x0 * sin_t + x1 * cos_t;
+    }
 }

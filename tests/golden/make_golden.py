@@ -16,6 +16,11 @@ Outputs:
   config1_decode.npz       The Llama-2-7B single-layer decode workload (32/32
       heads, D=128, context 512 + 1 appended token, 64-page permuted table):
       seed, SHA-256 of the regenerated inputs and the reference output.
+  rope_cases.npz           The reference's three RoPE tests
+      (tests/test_kernels.cu:718-780: inputs from its ``random_floats`` with
+      the same seeds, ranges, head dims and positions) and further positions
+      and head dims (64, 128, 256; positions up to 8191), each with the output
+      of its ``cpu_rope``.
 """
 import hashlib
 import os
@@ -28,6 +33,19 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 import oracle  # noqa: E402
 from tests.golden import gen  # noqa: E402
+
+# name, head_dim, lo, hi, seed, position, theta -- tests/test_kernels.cu:718-780 first
+ROPE_CASES = [
+    ("Position0_Identity", 64, -1.0, 1.0, 1100, 0, 10000.0),
+    ("PreservesNorm", 128, -2.0, 2.0, 1200, 42, 10000.0),
+    ("AgainstCPUReference", 128, -1.0, 1.0, 1300, 100, 10000.0),
+    ("d64_pos1", 64, -1.0, 1.0, 1400, 1, 10000.0),
+    ("d128_pos511", 128, -1.0, 1.0, 1401, 511, 10000.0),
+    ("d128_pos4095", 128, -0.5, 0.5, 1402, 4095, 10000.0),
+    ("d128_pos8191", 128, -1.0, 1.0, 1403, 8191, 10000.0),
+    ("d256_pos2048", 256, -1.0, 1.0, 1404, 2048, 10000.0),
+    ("d128_pos777_theta500k", 128, -1.0, 1.0, 1405, 777, 500000.0),
+]
 
 REF_CASES = [
     # name, B, H, S, D, lo, hi, seeds (q, k, v)  -- tests/test_attention.cu
@@ -92,6 +110,14 @@ def main():
     out = ref_decode_rows(c["pool"], g, 0, c["q"], c["bt"], c["lens"])
     np.savez_compressed(os.path.join(HERE, "config1_decode.npz"), seed=np.int64(gen.CONFIG1_SEED),
                         sha256=np.frombuffer(gen.digest(c).encode(), np.uint8), out=out)
+    arrays = {}
+    for name, d, lo, hi, seed, pos, theta in ROPE_CASES:
+        x = oracle.ref_kernels_random_floats(d, lo, hi, seed)
+        arrays[name + "/x"] = x
+        arrays[name + "/meta"] = np.array([d, pos], np.int32)
+        arrays[name + "/theta"] = np.float32(theta)
+        arrays[name + "/y"] = oracle.ref_rope(x, pos, theta)
+    np.savez_compressed(os.path.join(HERE, "rope_cases.npz"), **arrays)
     print("fixtures written to", HERE)
 
 

@@ -210,3 +210,29 @@ def test_model_compaction():
     pairs = m.compact_plan()
     assert pairs == [(9, 0), (8, 2), (7, 3)]
     assert [i for i, u in enumerate(m.in_use) if u] == list(range(6))
+
+
+def test_oracle_rope_matches_reference_golden():
+    """The oracle's RoPE restatement is bit-identical to the reference's own
+    cpu_rope (tests/test_kernels.cu:697-716) on its three tests' inputs and on
+    further head dims, positions and bases (tests/golden/rope_cases.npz)."""
+    z = np.load(os.path.join(GOLD, "rope_cases.npz"))
+    names = sorted({k.split("/")[0] for k in z.files})
+    assert len(names) >= 9
+    for name in names:
+        d, pos = (int(v) for v in z[name + "/meta"])
+        got = oracle.rope(z[name + "/x"][None], [pos], float(z[name + "/theta"]))[0]
+        assert np.array_equal(got.view(np.uint32), z[name + "/y"].view(np.uint32)), name
+
+
+def test_oracle_rope_properties():
+    """Position 0 is the identity and every rotated pair keeps its norm (the
+    reference's Position0_Identity and PreservesNorm tests)."""
+    z = np.load(os.path.join(GOLD, "rope_cases.npz"))
+    x0 = z["Position0_Identity/x"]
+    assert np.array_equal(oracle.rope(x0[None], [0])[0], x0)
+    x = z["PreservesNorm/x"]
+    y = oracle.rope(x[None], [42])[0]
+    n_in = np.hypot(x[0::2], x[1::2])
+    n_out = np.hypot(y[0::2], y[1::2])
+    assert np.abs(n_in - n_out).max() < 1e-4
