@@ -287,6 +287,17 @@ vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, void* out,
                      const int32_t* positions, int32_t batch, int32_t tokens,
                      int32_t num_q_heads, float scale, void* stream);
 
+/* Fused RoPE (VULCAN's rope kernel, cuda/rope.cu:34-60, applied to Q and to
+ * K_new before the append at src/transformer.cpp:114-128): with theta_base > 0
+ * the pool's kernels rotate each pair (2i, 2i+1) by
+ * pos / theta_base^(2i / head_dim) as they read it: vk_append and
+ * vk_append_f32 rotate K rows at their positions (V unchanged); vk_decode and
+ * vk_decode_run rotate q, and vk_decode_run its k_new, at the new token's
+ * position seq_len - 1; vk_prefill rotates q at positions[b] + t.  Callers
+ * then pass unrotated projections.  0 (the default) turns it off; head_dim
+ * must be even. */
+vk_status vk_set_rope(vk_pool* pool, float theta_base);
+
 /* Selects the prefill kernel for the pool: 0 = automatic (the tcgen05/TMEM
  * kernel for head_dim 128, the mma.sync kernel otherwise), 1 = the mma.sync
  * kernel, 2 = the tcgen05 kernel (VK_UNSUPPORTED from vk_prefill for other

@@ -73,6 +73,7 @@ SIGNATURES = {
     "vk_decode_plan_set_gather": (c_i32, [vp, vp, c_i32, c_i32]),
     "vk_prefill": (c_i32, [vp, c_i32, vp, vp, vp, c_i32, vp, c_i32, c_i32, c_i32, c_f32, vp]),
     "vk_set_prefill_path": (c_i32, [vp, c_i32]),
+    "vk_set_rope": (c_i32, [vp, c_f32]),
     "vk_copy_pages": (c_i32, [vp, vp, vp, c_i32, vp]),
     "vk_remap_block_tables": (c_i32, [vp, c_i64, vp, c_i32, vp]),
     "vk_compact_plan": (c_i32, [vp, i32p, i32p, c_i32, i32p]),

@@ -9,6 +9,7 @@
 // (token, kv head) covering its K row and V row.
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
+#include "vk_rope.cuh"
 
 namespace vk {
 
@@ -21,6 +22,7 @@ struct AppendParams {
     uint32_t* err;
     uint64_t seg_bytes, layer_off, head_bytes;
     int bt_stride, B, T, Hkv, D, P, num_pages;
+    const float* rope_freq;  // non-null: K rows are rotated (RoPE) at their positions
 };
 
 template <bool F32>
@@ -57,7 +59,15 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
             const float4* src =
                 reinterpret_cast<const float4*>(static_cast<const float*>(is_v ? p.v : p.k) + src_elem) +
                 2 * vi;
-            const float4 a = __ldg(src), c = __ldg(src + 1);
+            float4 a = __ldg(src), c = __ldg(src + 1);
+            if (!is_v && p.rope_freq != nullptr) {  // rotate in fp32, then round
+                const int i0 = vi * 4;
+                float2 r;
+                r = rope_pair(a.x, a.y, i0, pos, p.rope_freq); a.x = r.x; a.y = r.y;
+                r = rope_pair(a.z, a.w, i0 + 1, pos, p.rope_freq); a.z = r.x; a.w = r.y;
+                r = rope_pair(c.x, c.y, i0 + 2, pos, p.rope_freq); c.x = r.x; c.y = r.y;
+                r = rope_pair(c.z, c.w, i0 + 3, pos, p.rope_freq); c.z = r.x; c.w = r.y;
+            }
             val.x = pack_half2(a.x, a.y);
             val.y = pack_half2(a.z, a.w);
             val.z = pack_half2(c.x, c.y);
@@ -66,6 +76,7 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
             const uint4* src =
                 reinterpret_cast<const uint4*>(static_cast<const __half*>(is_v ? p.v : p.k) + src_elem) + vi;
             val = __ldg(src);
+            if (!is_v && p.rope_freq != nullptr) val = rope_uint4(val, vi * 8, pos, p.rope_freq);
         }
         reinterpret_cast<uint4*>(is_v ? dst_v : dst_k)[vi] = val;
     }
@@ -95,6 +106,7 @@ vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, 
     p.D = D;
     p.P = pool->cfg.page_tokens;
     p.num_pages = pool->num_pages;
+    p.rope_freq = pool->kv ? pool->rope_freq : nullptr;
     const int64_t threads = static_cast<int64_t>(B) * T * p.Hkv * 32;
     const int64_t blocks = (threads + 255) / 256;
     if (blocks > 0x7fffffff) return fail(VK_INVALID_ARG, "append too large for one launch");

@@ -30,6 +30,7 @@
 
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
+#include "vk_rope.cuh"
 
 namespace vk {
 
@@ -47,6 +48,7 @@ struct DecodeParams {
     uint32_t* err;
     int bt_stride, Hq, Hkv, G, L, layer, num_pages, pps, max_splits;
     float scale_log2;
+    const float* rope_freq;  // non-null: q rotated (RoPE) at position seq_len - 1
 };
 
 template <int D>
@@ -158,6 +160,16 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
                 qf[nt][ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
                 qf[nt][ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
             }
+        }
+        if (p.rope_freq != nullptr) {  // fused RoPE at the new token's position
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int d = ks * 16 + (lane & 3) * 2;
+                    qf[nt][ks][0] = rope_word(qf[nt][ks][0], d, seq_len - 1, p.rope_freq);
+                    qf[nt][ks][1] = rope_word(qf[nt][ks][1], d + 8, seq_len - 1, p.rope_freq);
+                }
         }
         const int g8 = lane >> 2;           // token row of this lane in S^T (and +8)
         const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix index, row in matrix
@@ -429,6 +441,7 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
     if (p.max_splits > 65535) return fail(VK_INVALID_ARG, "too many splits");
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;
+    p.rope_freq = pool->rope_freq;
     p.ws_o = nullptr;
     p.ws_lse = nullptr;
     if (p.max_splits > 1) {

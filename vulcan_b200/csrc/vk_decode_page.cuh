@@ -13,6 +13,7 @@
 #pragma once
 
 #include "vk_ptx.cuh"
+#include "vk_rope.cuh"
 
 namespace vk {
 
@@ -49,6 +50,21 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qf)[NT][D / 16][2], cons
             qf[nt][ks][1] = ok ? __ldg(reinterpret_cast<const unsigned int*>(qrow + d + 8)) : 0u;
         }
     }
+}
+
+// Fused RoPE of the q fragments loaded by load_q_frags (every query head of a
+// unit at the new token's position pos); freq == nullptr: no rotation.
+template <int D, int NT>
+__device__ __forceinline__ void rope_q_frags(uint32_t (&qf)[NT][D / 16][2], int pos, const float* freq, int lane) {
+    if (freq == nullptr) return;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+            const int d = ks * 16 + (lane & 3) * 2;
+            qf[nt][ks][0] = rope_word(qf[nt][ks][0], d, pos, freq);
+            qf[nt][ks][1] = rope_word(qf[nt][ks][1], d + 8, pos, freq);
+        }
 }
 
 // Folds one page held at shared address `sb` (valid tokens 1..16) into `st`.

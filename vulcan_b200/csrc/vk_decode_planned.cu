@@ -71,6 +71,7 @@ struct PlanParams {
     int bt_stride, Hq, Hkv, G, L, layer, num_pages, W, Z, U;
     int ntasks, S;   // merge tasks, tasks (head groups) per split unit
     int lmm;         // units of up to lmm pieces merge in their last piece (others: tasks)
+    const float* rope_freq;  // non-null: q and the new K rotated (RoPE) at the new token's position
     float scale_log2;
     // fused output gather (g.world == 0: none)
     GatherView g;
@@ -422,6 +423,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
     uint32_t qf[NT][KS][2];
     WarpSoftmaxState<D, NT> st;
     load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D, p.G, lane);
+    rope_q_frags<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
     st.reset();
 
     for (int j = 0; j < n; ++j) {
@@ -445,6 +447,8 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                 row_val[i] = v < 2 * NCH ? __ldg(reinterpret_cast<const uint4*>((is_v ? p.v_new : p.k_new) + src) +
                                                  (is_v ? v - NCH : v))
                                          : make_uint4(0, 0, 0, 0);
+                if (v < NCH && p.rope_freq != nullptr)  // the new K row, rotated at its position
+                    row_val[i] = rope_uint4(row_val[i], v * 8, p.ulen[cu.u] - 1, p.rope_freq);
             }
         }
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), (j / NS) & 1, p.err))) return;
@@ -550,6 +554,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                 cu.next(p.uoff);
                 load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D,
                                     p.G, lane);
+                rope_q_frags<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
                 st.reset();
             }
         } else {
@@ -878,6 +883,7 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     p.ntasks = plan->ntasks;
     p.S = plan->S;
     p.lmm = plan->lmm;
+    p.rope_freq = pool->rope_freq;
     p.zunits = t + plan->o_z;
     p.counters = reinterpret_cast<uint32_t*>(ws + plan->counters_off);
     p.part_o = reinterpret_cast<float*>(ws + plan->part_o_off);

@@ -53,6 +53,8 @@ struct vk_pool {
     int32_t prefill_path = 0;        // 0 auto, 1 mma.sync kernel, 2 tcgen05 kernel
     int32_t split_override = 0;
     int32_t plan_workers = 0;        // cap on planned-decode workers (0 = resident warps)
+    float rope_theta = 0.f;          // fused RoPE base (0 = off)
+    float* rope_freq = nullptr;      // device [head_dim/2] frequencies when RoPE is on
     int32_t num_sms = vk::kNumSmsDefault;
     vk::Allocator alloc;
 };

@@ -256,6 +256,7 @@ vk_status vk_pool_destroy(vk_pool* pool) {
     DeviceGuard g(pool->device);
     if (pool->owns_mem && pool->base) cudaFree(pool->base);
     if (pool->d_err) cudaFree(pool->d_err);
+    if (pool->rope_freq) cudaFree(pool->rope_freq);
     delete pool;
     return VK_OK;
 }

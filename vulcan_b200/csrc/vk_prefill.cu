@@ -16,8 +16,12 @@
 //    S accumulator is re-used as the A operand of P V in registers; online
 //    softmax per row with quad shuffles; causal masking only on tiles that cross
 //    the diagonal; V of slots beyond the written tokens is zeroed in registers.
+#include <cmath>
+#include <vector>
+
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
+#include "vk_rope.cuh"
 
 namespace vk {
 
@@ -35,6 +39,7 @@ struct PrefillParams {
     uint32_t* err;
     int bt_stride, T, Hq, Hkv, G, L, layer, num_pages, q_tiles;
     float scale_log2;
+    const float* rope_freq;  // non-null: q rotated (RoPE) at its position
 };
 
 template <int D>
@@ -130,6 +135,12 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
                 qa[ks][1] = vhi ? __ldg(reinterpret_cast<const unsigned int*>(qhi + d)) : 0u;
                 qa[ks][2] = vlo ? __ldg(reinterpret_cast<const unsigned int*>(qlo + d + 8)) : 0u;
                 qa[ks][3] = vhi ? __ldg(reinterpret_cast<const unsigned int*>(qhi + d + 8)) : 0u;
+                if (p.rope_freq != nullptr) {
+                    qa[ks][0] = rope_word(qa[ks][0], d, qpos_lo, p.rope_freq);
+                    qa[ks][1] = rope_word(qa[ks][1], d, qpos_hi, p.rope_freq);
+                    qa[ks][2] = rope_word(qa[ks][2], d + 8, qpos_lo, p.rope_freq);
+                    qa[ks][3] = rope_word(qa[ks][3], d + 8, qpos_hi, p.rope_freq);
+                }
             }
         }
         float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
@@ -303,6 +314,7 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
     p.layer = layer;
     p.num_pages = pool->num_pages;
     p.q_tiles = (tokens + kPreRows - 1) / kPreRows;
+    p.rope_freq = pool->rope_freq;
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;
     DeviceGuard g(pool->device);
@@ -313,6 +325,38 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
         return prefill_tc(pool, layer, q, out, block_tables, bt_stride, positions, batch, tokens, num_q_heads, scale,
                           st);
     return D == 128 ? launch_prefill_t<128>(pool, p, batch, st) : launch_prefill_t<64>(pool, p, batch, st);
+}
+
+extern "C" vk_status vk_set_rope(vk_pool* pool, float theta_base) {
+    if (!pool) return fail(VK_INVALID_ARG, "pool is NULL");
+    if (!(theta_base >= 0.f) || theta_base == 1.0f) return fail(VK_INVALID_ARG, "RoPE base must be 0 (off) or > 0 and != 1");
+    if (theta_base == 0.f) {
+        pool->rope_theta = 0.f;
+        if (pool->rope_freq) {
+            DeviceGuard g(pool->device);
+            cudaFree(pool->rope_freq);
+            pool->rope_freq = nullptr;
+        }
+        return VK_OK;
+    }
+    if (!pool->kv || (pool->cfg.head_dim & 1)) return fail(VK_UNSUPPORTED, "RoPE needs a KV pool with an even head_dim");
+    // frequencies with cpu_rope's float steps (tests/test_kernels.cu:703-705)
+    const int D = pool->cfg.head_dim, half = D / 2;
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; ++i)
+        freq[i] = 1.0f / std::pow(theta_base, 2.0f * static_cast<float>(i) / static_cast<float>(D));
+    DeviceGuard g(pool->device);
+    if (!pool->rope_freq) {
+        cudaError_t e = cudaMalloc(&pool->rope_freq, sizeof(float) * half);
+        if (e != cudaSuccess) {
+            pool->rope_freq = nullptr;
+            return cuda_fail(e, "cudaMalloc(RoPE table)");
+        }
+    }
+    cudaError_t e = cudaMemcpy(pool->rope_freq, freq.data(), sizeof(float) * half, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(RoPE table)");
+    pool->rope_theta = theta_base;
+    return VK_OK;
 }
 
 extern "C" vk_status vk_set_prefill_path(vk_pool* pool, int32_t path) {

@@ -32,6 +32,7 @@
 //    cannot reach O.  All waits are bounded.
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
+#include "vk_rope.cuh"
 
 namespace vk {
 
@@ -55,6 +56,7 @@ struct TcParams {
     uint32_t* err;
     int bt_stride, T, Hq, Hkv, G, layer, num_pages, q_tiles;
     float scale_log2;
+    const float* rope_freq;  // non-null: q rotated (RoPE) at its position
 };
 
 // ---------------------------------------------------------------- tcgen05 PTX
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 uint4 v = valid_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                if (p.rope_freq != nullptr) v = rope_uint4(v, c * 8, qpos, p.rope_freq);
                 const uint32_t addr =
                     sbase + kTcQ + t * 32768 + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
                 asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
@@ -513,6 +516,7 @@ vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const i
     p.q_tiles = (T + 2 * kTcRows - 1) / (2 * kTcRows);
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(kTcD));
     p.scale_log2 = sc * 1.4426950408889634f;
+    p.rope_freq = pool->rope_freq;
     return launch_prefill_tc(pool, p, B, st);
 }
 

@@ -169,6 +169,10 @@ class PagedKVPool:
     def set_split(self, pages_per_split: int) -> None:
         check(self._lib.vk_set_decode_split(self.handle, pages_per_split), "vk_set_decode_split")
 
+    def set_rope(self, theta_base: float) -> None:
+        """Fused RoPE in append, decode and prefill (see vk_set_rope); 0 = off."""
+        check(self._lib.vk_set_rope(self.handle, float(theta_base)), "vk_set_rope")
+
     def set_plan_workers(self, max_workers: int) -> None:
         """Caps the workers of plans made afterwards (0 = one per resident warp)."""
         check(self._lib.vk_set_decode_workers(self.handle, max_workers), "vk_set_decode_workers")
