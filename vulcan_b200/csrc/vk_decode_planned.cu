@@ -7,10 +7,11 @@
 //
 //  * The plan (host, once per decode step since every layer of a step has the
 //    same lengths) lays the pages of all (sequence, KV head) units end to end
-//    and cuts that list into W equal contiguous ranges, one per warp ("worker"),
-//    with W = resident warps of the GPU.  Every worker streams the same number
-//    of pages, so there is no tail of long sequences and no per-split CTA
-//    prologue; ranges cross unit boundaries freely.
+//    and cuts that list into W contiguous ranges of equal cost, one per warp
+//    ("worker"), with W = resident warps of the GPU: a page costs 1 and the end
+//    of a unit inside a range (fused append, partial, next q) costs 6, so no
+//    worker is a straggler; there is no tail of long sequences and no
+//    per-split CTA prologue; ranges cross unit boundaries freely.
 //  * Each worker warp prefetches its own pages NSTW ahead with 2-D TMA loads
 //    (one mbarrier per stage) and folds each page into its softmax state with
 //    the tensor-core page update shared with vk_decode.
@@ -44,6 +45,8 @@ namespace vk {
 constexpr int kPlanWarps = 2;      // worker warps per CTA
 constexpr int kPlanStages = 4;     // TMA stages per worker (8 KiB each at D=128)
 constexpr int kMinPagesPerWorker = 8;
+constexpr int64_t kUnitEndPages = 6;  // cost of a unit end inside a worker range, in pages (measured best of 0-16)
+constexpr int64_t kUnitEndScale = 1;
 constexpr int kLastMergeMax = 8;   // large shares: units of up to this many pieces merge in their last piece
 constexpr int kLastMergeMinPages = 64;  // ... when workers have at least this many pages
 
@@ -691,7 +694,33 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
 
     // worker ranges and the unit each starts in
     std::vector<int32_t> wb(static_cast<size_t>(W) + 1), wfu(static_cast<size_t>(W));
-    for (int64_t w = 0; w <= W; ++w) wb[w] = static_cast<int32_t>(W ? (w * T) / W : 0);
+    // Equal cost rather than equal pages: the end of a unit inside a range
+    // (the fused append, the piece's partial and the next unit's q) costs
+    // about kUnitEndPages pages of streaming, so ranges that hold unit ends get
+    // fewer pages.  Every range keeps at least one page.
+    if (W > 0) {
+        std::vector<int64_t> uend;  // page index just past each non-empty unit
+        for (int u = 0; u < U; ++u)
+            if (uoff[u + 1] > uoff[u]) uend.push_back(uoff[u + 1]);
+        auto cost_before = [&](int64_t g) {  // pages before g plus ends of units finished before g
+            const int64_t ends = std::upper_bound(uend.begin(), uend.end(), g) - uend.begin();
+            return g * kUnitEndScale + ends * kUnitEndPages * kUnitEndScale;
+        };
+        const int64_t total = cost_before(T);
+        for (int64_t w = 0; w <= W; ++w) {
+            const int64_t target = total * w / W;
+            int64_t lo = 0, hi = T;  // smallest g with cost_before(g) >= target
+            while (lo < hi) {
+                const int64_t mid = (lo + hi) / 2;
+                if (cost_before(mid) >= target) hi = mid; else lo = mid + 1;
+            }
+            wb[w] = static_cast<int32_t>(lo);
+        }
+        wb[0] = 0;
+        wb[W] = static_cast<int32_t>(T);
+        for (int64_t w = 1; w < W; ++w) wb[w] = std::max<int32_t>(wb[w], wb[w - 1] + 1);
+        for (int64_t w = W - 1; w >= 1; --w) wb[w] = std::min<int32_t>(wb[w], wb[w + 1] - 1);
+    }
     {
         int u = 0;
         for (int64_t w = 0; w < W; ++w) {
