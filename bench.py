@@ -115,6 +115,22 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
+# the committed ncu captures, for the workloads they were taken on.
+NCU_DECODE_70B_BYTES = 590.999296e6 + 4.925184e6   # profiles/planned_decode_kernel_70b-one-layer_full.md
+NCU_PREFILL_2SEQ_BYTES = 190.358528e6 + 4.508928e6  # profiles/prefill_tc_kernel_small-case_full.md
+
+
+def prefill_tile_reads(ctx, T, rows=256, keys=128):
+    """K/V tiles the tcgen05 prefill reads per head: one pass over the keys of
+    each 256-row CTA (keys up to the CTA's last row)."""
+    n = 0
+    for p in np.asarray(ctx).tolist():
+        for q0 in range(0, T, rows):
+            n += (p + min(T, q0 + rows) + keys - 1) // keys
+    return n
+
+
 # ----------------------------------------------------------------------------- clocks
 
 class ClockSampler:
@@ -455,6 +471,12 @@ def main():
             dec_src = "step time / layers (events unavailable)"
     clocks = clk.summary()
 
+    # --- DRAM traffic per launch from the committed ncu capture (70B, 1 GPU, planned)
+    traffic, traffic_src = None, None
+    if (args.config == "70b" and world == 1 and args.path == "planned" and not args.layers and not args.batch):
+        traffic = NCU_DECODE_70B_BYTES
+        traffic_src = "ncu capture of one launch: profiles/planned_decode_kernel_70b-one-layer_full.md"
+
     # --- algorithmic bytes (this rank's share) and roofline of the decode launch
     ab_local = algorithmic_bytes(ctx, hq_l, hkv_l, D)
     peak, peak_kind = measured_peaks()
@@ -509,7 +531,7 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
                          "kernel": ("vk_decode_run (planned: append + decode + merge in one launch)"
                                     if args.path == "planned" else "vk_decode (split grid + merge)"),
                          "peak_source": peak_kind, "launch_ms": dec_avg_ms, "launch_timing": dec_src,
@@ -748,6 +770,11 @@ def run_prefill(args, wl):
     launch_ms = sum(a.elapsed_time(b) for a, b in ev) / L
     flops_local = prefill_flops(ctx, T, H, D)
     flops_job = prefill_flops(wl["ctx"], T, H, D)
+    # ncu traffic of the 2-sequence capture scaled by the K/V tiles this launch reads
+    full_wl = workload("prefill")
+    traffic = NCU_PREFILL_2SEQ_BYTES * prefill_tile_reads(ctx, T) / prefill_tile_reads(full_wl["ctx"][:2], T)
+    traffic_src = ("ncu capture of the first 2 sequences (1 layer), scaled by K/V tiles read: "
+                   "profiles/prefill_tc_kernel_small-case_full.md")
     peak_t = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     achieved = flops_local / (launch_ms * 1e-3) / 1e12
@@ -761,7 +788,8 @@ def run_prefill(args, wl):
                 "attn_tflops": flops_job * L / (ms_step * 1e-3) / 1e12,
                 "gpu_launches": 2 * L * args.steps, "clocks": clk.summary(),
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
-                             "frac": achieved / peak_t, "traffic": None, "kernel": "vk_prefill",
+                             "frac": achieved / peak_t, "traffic": traffic, "traffic_source": traffic_src,
+                             "kernel": "vk_prefill",
                              "launch_ms": launch_ms, "flops_per_launch": flops_local}}
         print(json.dumps(line), flush=True)
     del graph
