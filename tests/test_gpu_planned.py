@@ -127,7 +127,7 @@ def test_planned_fused_gather_one_rank(vk):
     """A gather of one rank: every layer's output lands in slot slot_base +
     layer of the receive buffer, bit-identical to the plain run, with and
     without an explicit `out`, with and without the previous-slot wait;
-    vk_gather_wait passes and no timeout is recorded."""
+    vk_decode_plan_gather_wait passes and no timeout is recorded."""
     rng = np.random.default_rng(31)
     lens = np.array([0, 1, 17, 300, 2049], np.int32)
     Hq, Hkv, D, L = 16, 2, 128, 3

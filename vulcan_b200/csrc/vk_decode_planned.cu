@@ -46,7 +46,6 @@ constexpr int kPlanWarps = 2;      // worker warps per CTA
 constexpr int kPlanStages = 4;     // TMA stages per worker (8 KiB each at D=128)
 constexpr int kMinPagesPerWorker = 8;
 constexpr int64_t kUnitEndPages = 6;  // cost of a unit end inside a worker range, in pages (measured best of 0-16)
-constexpr int64_t kUnitEndScale = 1;
 constexpr int kLastMergeMax = 8;   // large shares: units of up to this many pieces merge in their last piece
 constexpr int kLastMergeMinPages = 64;  // ... when workers have at least this many pages
 
@@ -704,7 +703,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
             if (uoff[u + 1] > uoff[u]) uend.push_back(uoff[u + 1]);
         auto cost_before = [&](int64_t g) {  // pages before g plus ends of units finished before g
             const int64_t ends = std::upper_bound(uend.begin(), uend.end(), g) - uend.begin();
-            return g * kUnitEndScale + ends * kUnitEndPages * kUnitEndScale;
+            return g + ends * kUnitEndPages;
         };
         const int64_t total = cost_before(T);
         for (int64_t w = 0; w <= W; ++w) {
