@@ -802,9 +802,12 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             lens_host, plan_ws, use_graph, gat=None):
     """Same step through the public API with host buffers: each layer's q/k/v is
     copied from pinned host memory to the device on a copy stream (double
-    buffered, overlapping the previous layer's kernel) and each layer's output
-    is copied back to pinned host memory on a second copy stream, all inside
-    the timed region.  At N=1 the step is one CUDA graph."""
+    buffered, overlapping the previous layer's kernel; they stand in for the
+    projections a model computes on the device), and the step's result, the
+    last layer's (all-gathered) attention output, is copied back to pinned host
+    memory on a second copy stream, all inside the timed region.  Earlier
+    layers' outputs stay on the device, as in a model where they feed the next
+    layer.  At N=1 the step is one CUDA graph."""
     import torch
     import torch.distributed as dist
     g = torch.Generator()
@@ -813,7 +816,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     hk = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
     hv = (torch.randn(L, Bl, hkv_l, D, generator=g) * 0.5).half().pin_memory()
     gathered_host = gathered is not None or gat is not None
-    out_shape = (L, world, Bl, hq_l, D) if gathered_host else (L, Bl, hq_l, D)
+    out_shape = (world, Bl, hq_l, D) if gathered_host else (Bl, hq_l, D)
     hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
     nbuf = 2
     dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
@@ -875,14 +878,16 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             fe = torch.cuda.Event()
             fe.record(cur)
             freed[s] = fe
+            last = l == L - 1
             if gat is not None:
-                # slot l-1 is complete once run l (which waited for it) is done
-                # the copy stream waits for every rank's slice of this layer
-                # (a bounded flag wait on peers' stores), then reads the slot
-                d2h.wait_event(fe)
-                with torch.cuda.stream(d2h):
-                    plan.gather_wait(l, stream=d2h)
-                    hout[l].copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
+                if last:
+                    # the copy stream waits for every rank's slices of the last
+                    # layer (ranks raise their flags in layer order, so this
+                    # covers the step), then reads the slot
+                    d2h.wait_event(fe)
+                    with torch.cuda.stream(d2h):
+                        plan.gather_wait(l, stream=d2h)
+                        hout.copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
             elif gathered_host:
                 comm.wait_event(fe)
                 with torch.cuda.stream(comm):
@@ -894,9 +899,9 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             else:
                 d2h.wait_event(fe)
                 src = douts[s]
-            if gat is None:
+            if gat is None and last:
                 with torch.cuda.stream(d2h):
-                    hout[l].copy_(src, non_blocking=True)
+                    hout.copy_(src, non_blocking=True)
                     od = torch.cuda.Event()
                     od.record(d2h)
                     outdone[s] = od
@@ -958,7 +963,8 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     del graph, graphs
     return {"ms_step": ms / args.steps, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h_bytes),
-            "path": "PagedKVPool / DecodePlan (C ABI) with pinned host q, k, v and outputs; H2D and D2H on "
+            "path": "PagedKVPool / DecodePlan (C ABI): every layer's q, k, v from pinned host memory, the "
+                    "step's result (last layer's gathered output) back to pinned host memory; H2D and D2H on "
                     "copy streams inside the timed region" + ("; CUDA graph per step" if use_graph else "")}
 
 
