@@ -12,9 +12,10 @@
 //    of a unit inside a range (fused append, partial, next q) costs 6, so no
 //    worker is a straggler; there is no tail of long sequences and no
 //    per-split CTA prologue; ranges cross unit boundaries freely.
-//  * Each worker warp prefetches its own pages NSTW ahead with 2-D TMA loads
-//    (one mbarrier per stage) and folds each page into its softmax state with
-//    the tensor-core page update shared with vk_decode.
+//  * Each worker warp prefetches its own pages kPlanStages ahead with 2-D TMA
+//    loads (one mbarrier per stage; the block-table entries of the next 32
+//    pages read in one coalesced round trip) and folds each page into its
+//    softmax state with the tensor-core page update shared with vk_decode.
 //  * Append fused: the last page of a unit is loaded as it is; when new K/V
 //    rows were given, the consuming warp stores them into the pool and patches
 //    them into the staged copy before folding the page in, so no load waits for
@@ -27,12 +28,16 @@
 //    at the same time) are merged by tasks of (unit, group of query heads)
 //    dealt to all warps of the grid by the plan; a warp runs its tasks after
 //    its own page range, each once the unit's pieces are all counted
-//    (bounded wait).  No warp merges in the middle of its range, and the merge
-//    of a unit split into many pieces is spread over up to G warps.
-//  * Gather fused (optional, head-sharded multi-GPU): each finished unit output
-//    is also stored into every rank's receive slice over NVLink; the warp that
-//    counts the layer's last unit raises this rank's flag on every rank.  A run
-//    may first wait for all ranks' flags of the previous layer's slot.
+//    (bounded wait).  The merge of a unit split into many pieces is thus
+//    spread over up to G warps.
+//  * Gather fused (optional, head-sharded multi-GPU): each finished output is
+//    also stored into every rank's receive slice over NVLink with plain peer
+//    stores.  The next run on the stream, which starts after this grid has
+//    completed, raises this rank's flag of that slot on every rank (step
+//    epoch, one system fence); in strict order a run first waits for all
+//    ranks' flags of the previous layer's slot.
+//  * RoPE fused (optional): q and the new K rows are rotated in registers as
+//    they are loaded (vk_rope.cuh).
 #include <algorithm>
 #include <vector>
 
@@ -59,7 +64,7 @@ struct PlanParams {
     const int32_t* uslot;  // [U]   first partial slot of the unit (-1 if one piece)
     const int32_t* tunits; // [ntasks / S] unit of each merge task group
     const int32_t* zunits; // [Z]   units without pages (zero output)
-    uint32_t* counters;    // [2U] pieces finished, merge tasks finished (reset by the last task)
+    uint32_t* counters;    // [2U] pieces finished, merge tasks finished (reset by the merger / last task)
     float* part_o;         // [slots, G, D]
     float* part_lse;       // [slots, G]
     const __half* q;
