@@ -288,6 +288,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
             tc_fence_after();
             const int nt[2] = {ntA, ntB};
             int k_waited = -1;  // highest key tile whose K stage has been waited for
+            // Descriptors are formed once; within a tile only the start-address
+            // field moves (by constants), so each MMA costs one add at issue:
+            // the issuing warp shares its SM sub-partition with two softmax
+            // warps, and every issue slot it spends delays the tensor pipe.
+            const uint64_t dq0 = umma_desc_sw128(sbase + kTcQ, 16, 1024);
+            const uint64_t dk0 = umma_desc_sw128(sbase + kTcK, 16, 1024);
+            const uint64_t dv0 = umma_desc_sw128(sbase + kTcV, 16384, 1024);
             auto issue_s = [&](int t, int j) {
                 const int st = j & 1;
                 if (j > k_waited) {
@@ -296,11 +303,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                 }
                 if (!ok) return;
                 tc_fence_after();
+                const uint64_t dq = dq0 + static_cast<uint64_t>(t * (32768 >> 4));
+                const uint64_t dk = dk0 + static_cast<uint64_t>(st * (32768 >> 4));
+                const uint32_t dt = tmem + t * 128;
 #pragma unroll
                 for (int ks = 0; ks < kTcD / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-                    umma_ss(tmem + t * 128, umma_desc_sw128(sbase + kTcQ + t * 32768 + off, 16, 1024),
-                            umma_desc_sw128(sbase + kTcK + st * 32768 + off, 16, 1024), id_s, ks > 0);
+                    const uint64_t off = ((ks >> 2) * 16384 + (ks & 3) * 32) >> 4;
+                    umma_ss(dt, dq + off, dk + off, id_s, ks > 0);
                 }
                 umma_commit(smem_u32(&s_full[t]));
                 // the last S that reads this K stage releases it
@@ -312,11 +321,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                 if (t == 0 || j >= ntA) ok = ok && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
                 if (!ok) return;
                 tc_fence_after();
+                const uint64_t dv = dv0 + static_cast<uint64_t>(st * (32768 >> 4));
+                const uint32_t dpo = tmem + 256 + t * 128, dpa = tmem + t * 128;
+                umma_ts(dpo, dpa, dv, id_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-                for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-                    const uint64_t bv = umma_desc_sw128(sbase + kTcV + st * 32768 + ks * 2048, 16384, 1024);
-                    umma_ts(tmem + 256 + t * 128, tmem + t * 128 + ks * 8, bv, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
-                }
+                for (int ks = 1; ks < kTcKeys / 16; ++ks)
+                    umma_ts(dpo, dpa + ks * 8, dv + static_cast<uint64_t>(ks * (2048 >> 4)), id_pv, 1u);
                 umma_commit(smem_u32(&o_full[t]));
                 if (t == 1 || j >= ntB) umma_commit(smem_u32(&v_empty[st]));
             };
