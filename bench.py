@@ -96,12 +96,14 @@ def layout(ctx, seed, slack=1.2):
     return bt, num_pages
 
 
-def algorithmic_bytes(ctx, Hq, Hkv, D):
+def algorithmic_bytes(ctx, Hq, Hkv, D, kv_format="fp16"):
     """Bytes one layer of one step must move (counted once): K/V read, new K/V
-    read+write, Q read + O write, block-table reads."""
+    read (fp16) + write (page format), Q read + O write, block-table reads.
+    FP8 pages hold 2*D code bytes + 8 scale bytes per (token, head)."""
     lens = ctx + 1
-    kv = int((2 * lens * Hkv * D * 2).sum())
-    new = len(ctx) * 2 * Hkv * D * 2 * 2
+    row = 2 * D * 2 if kv_format == "fp16" else 2 * D + 8
+    kv = int((lens * Hkv * row).sum())
+    new = len(ctx) * Hkv * (2 * D * 2 + row)
     qo = len(ctx) * 2 * Hq * D * 2
     table = int((4 * ((lens + PAGE - 1) // PAGE)).sum())
     return dict(decode=kv + qo + table, append=new, total=kv + new + qo + table)
@@ -269,6 +271,8 @@ def main():
                     help="head-sharded output allgather: peer stores fused into the decode, overlapping the "
                          "next layer (p2p) or waited for before the next layer reads its inputs (p2p-wait); "
                          "or NCCL on a side stream")
+    ap.add_argument("--kv", default="fp16", choices=["fp16", "fp8"],
+                    help="page format of the decode configs: fp16, or e4m3 codes with an fp32 scale per row")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
     ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
     args = ap.parse_args()
@@ -324,16 +328,28 @@ def main():
     max_len = int(lens.max())
 
     # --- pool and inputs on the device
-    pool = vk.PagedKVPool(L, hkv_l, D, num_pages, own_memory=False, zero=False)
+    pool = vk.PagedKVPool(L, hkv_l, D, num_pages, own_memory=False, zero=False, kv_format=args.kv)
     if args.pps:
         pool.set_split(args.pps)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000 + rank)
-    flat = pool.storage.view(torch.float16)
-    chunk = 1 << 28
-    for s in range(0, flat.numel(), chunk):
-        part = flat[s:s + chunk]
-        part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    if args.kv == "fp16":
+        flat = pool.storage.view(torch.float16)
+        chunk = 1 << 28
+        for s in range(0, flat.numel(), chunk):
+            part = flat[s:s + chunk]
+            part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    else:
+        # e4m3 codes of N(0, 0.5^2) rows at the scale of their quantisation
+        # (max|x| ~ 1.4 over 128 values), every code finite
+        blocks = pool.block_view().view(-1, pool.block_bytes)
+        codes_b = 2 * PAGE * D
+        for s in range(0, blocks.shape[0], 1 << 16):
+            part = blocks[s:s + (1 << 16)]
+            x = torch.randn(part.shape[0], codes_b, device=dev, generator=gen) * (0.5 * 448.0 / 1.4)
+            part[:, :codes_b].copy_(x.clamp_(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8))
+            sc = torch.full((part.shape[0], 2 * PAGE), 1.4 / 448.0, device=dev, dtype=torch.float32)
+            part[:, codes_b:].copy_(sc.view(torch.uint8))
     bt_d = torch.from_numpy(bt).to(dev)
     pos_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     lens_d = torch.from_numpy(lens).to(dev)
@@ -473,15 +489,16 @@ def main():
 
     # --- DRAM traffic per launch from the committed ncu capture (70B, 1 GPU, planned)
     traffic, traffic_src = None, None
-    if (args.config == "70b" and world == 1 and args.path == "planned" and not args.layers and not args.batch):
+    if (args.config == "70b" and world == 1 and args.path == "planned" and not args.layers and not args.batch
+            and args.kv == "fp16"):
         traffic = NCU_DECODE_70B_BYTES
         traffic_src = "ncu capture of one launch: profiles/planned_decode_kernel_70b-one-layer_full.md"
 
     # --- algorithmic bytes (this rank's share) and roofline of the decode launch
-    ab_local = algorithmic_bytes(ctx, hq_l, hkv_l, D)
+    ab_local = algorithmic_bytes(ctx, hq_l, hkv_l, D, args.kv)
     peak, peak_kind = measured_peaks()
     achieved = ab_local["decode"] / (dec_avg_ms * 1e-3) / 1e9
-    ab_job = algorithmic_bytes(ctx_all, Hq, Hkv, D)
+    ab_job = algorithmic_bytes(ctx_all, Hq, Hkv, D, args.kv)
     job_gbs = ab_job["total"] * L / (ms_step * 1e-3) / 1e9
     tokens_s = B / (ms_step * 1e-3)
 
@@ -509,9 +526,10 @@ def main():
         line = {
             "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16" if args.kv == "fp16" else "e4m3 K/V pages (fp32 scale per 128-value row), f16 Q/O, f32 accumulation",
             "data": "synthetic (seeded N(0,0.5^2) fp16 K/V/Q, random block tables)",
-            "config": {"workload": wl["desc"], "shard": wl["shard"] if world > 1 else "none",
+            "config": {"workload": wl["desc"], "kv_format": args.kv, "shard": wl["shard"] if world > 1 else "none",
                        "parallelism": ("kv-head shard x%d + %s" % (world, "allgather fused into the decode "
                                                                       "(peer stores over NVLink, flag per layer)"
                                                                       + (", each layer waits for the previous "

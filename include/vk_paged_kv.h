@@ -85,6 +85,29 @@ vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool);
 vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t bytes,
                             vk_pool** out_pool);
 
+/* ---- quantised KV pages ---------------------------------------------------
+ * VK_KV_FP16: the fp16 layout above (vk_pool_create, vk_pool_create_in).
+ * VK_KV_FP8: e4m3 codes with one fp32 scale per group of head_dim values (one
+ * token's K or V row of one head), the group-wise symmetric format of the
+ * reference's ADR-003 (docs/ADRs/003-quantization-format.md:11-18: scale =
+ * max|group| / qmax, value = code * scale) with qmax = 448.  Each (layer,
+ * page, head) block is 2*16*D + 128 bytes: K codes [16][D] with the 16-byte
+ * chunks of token t's row rotated by XOR (t & 7), V codes [D][16] with the
+ * tokens of a row in the order 0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15, then 16
+ * K and 16 V scales.  head_dim 128 and page_tokens 16 only.  FP8 pools take
+ * vk_append, vk_append_f32 (quantising), the planned decode (vk_decode_plan_*,
+ * vk_decode_run, fused append included), allocation, copy and swap; the other
+ * attention entry points return VK_UNSUPPORTED. */
+#define VK_KV_FP16 0
+#define VK_KV_FP8  1
+
+/* vk_pool_create (device_mem NULL) or vk_pool_create_in (device_mem given)
+ * with a page format; cfg->page_bytes must be 0. */
+vk_status vk_pool_create_fmt(const vk_pool_cfg* cfg, int32_t kv_format, void* device_mem, size_t bytes,
+                             vk_pool** out_pool);
+/* VK_KV_FP16 or VK_KV_FP8; -1 for a byte-page pool or NULL. */
+int32_t   vk_pool_kv_format(const vk_pool* pool);
+
 vk_status vk_pool_destroy(vk_pool* pool);
 
 /* Base device pointer, bytes per page and page count of the pool. */

@@ -57,6 +57,12 @@ def lib():
         L.or_remap_block_tables.argtypes = [_i32p, ctypes.c_int64, _i32p, _c_int]
         L.or_remap_block_tables.restype = None
         L.or_rope.argtypes = [_f32p, _f32p, _c_int, _c_int, ctypes.c_float]
+        L.or_e4m3_encode_array.argtypes = [_f32p, _u8p, ctypes.c_int64]
+        L.or_e4m3_decode_array.argtypes = [_u8p, _f32p, ctypes.c_int64]
+        L.or_fp8_quant_row.argtypes = [_f32p, _c_int, _u8p, ctypes.POINTER(ctypes.c_float)]
+        L.or_append_fp8.argtypes = ([_u8p] + [_c_int] * 6 + [_f32p, _f32p, _i32p, _c_int, _i32p, _c_int, _c_int])
+        L.or_append_fp8.restype = _c_int
+        L.or_dequant_fp8.argtypes = [_u8p] + [_c_int] * 5 + [_f32p]
         L.or_rope.restype = None
         _LIB = L
     return _LIB
@@ -231,4 +237,85 @@ def ref_kernels_random_floats(n, lo, hi, seed):
     R = ref_lib()
     out = np.empty(n, np.float32)
     R.ref_kernels_random_floats(n, lo, hi, seed, out)
+    return out
+
+
+# ---------------------------------------------------------------- FP8 pages
+# (group-wise symmetric quantisation of docs/ADRs/003-quantization-format.md:11-18
+# with an OCP E4M3 element; block layout in vk_oracle.c)
+
+FP8_QMAX = 448.0
+
+
+def fp8_block_bytes(D, P=16):
+    return 2 * P * D + 8 * P
+
+
+def e4m3_encode(x):
+    """Nearest-even E4M3 codes of fp32 values, finite overflow saturated to +-448."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.shape, np.uint8)
+    lib().or_e4m3_encode_array(x.reshape(-1), out.reshape(-1), x.size)
+    return out
+
+
+def e4m3_decode(c):
+    c = np.ascontiguousarray(c, np.uint8)
+    out = np.empty(c.shape, np.float32)
+    lib().or_e4m3_decode_array(c.reshape(-1), out.reshape(-1), c.size)
+    return out
+
+
+def fp8_quant_row(x):
+    """(codes uint8 [n], scale float32) of one group."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    codes = np.empty(x.size, np.uint8)
+    sc = ctypes.c_float()
+    lib().or_fp8_quant_row(x, x.size, codes, ctypes.byref(sc))
+    return codes, np.float32(sc.value)
+
+
+def append_fp8(pool_u8, g: Geom, layer, k, v, block_tables, positions):
+    """In-place append of fp32 (or fp16, widened exactly) rows [B, T, Hkv, D] into
+    a host byte image of an FP8 pool; returns 0 or -1 (bad entry skipped)."""
+    k = np.ascontiguousarray(np.asarray(k).astype(np.float32))
+    v = np.ascontiguousarray(np.asarray(v).astype(np.float32))
+    B, T = k.shape[0], k.shape[1]
+    flat = pool_u8.reshape(-1)
+    assert np.shares_memory(flat, pool_u8)
+    return lib().or_append_fp8(flat, g.L, g.Hkv, g.D, g.P, g.num_pages, layer, k.reshape(-1), v.reshape(-1),
+                               np.ascontiguousarray(block_tables, np.int32).reshape(-1), block_tables.shape[1],
+                               np.ascontiguousarray(positions, np.int32), B, T)
+
+
+def dequant_fp8(pool_u8, g: Geom):
+    """fp32 [L, num_pages, Hkv, 2, P, D]: code * scale of every slot."""
+    out = np.empty((g.L, g.num_pages, g.Hkv, 2, g.P, g.D), np.float32)
+    lib().or_dequant_fp8(np.ascontiguousarray(pool_u8).reshape(-1), g.L, g.Hkv, g.D, g.P, g.num_pages,
+                         out.reshape(-1))
+    return out
+
+
+def decode_fp8(pool_u8, g: Geom, layer, q, block_tables, seq_lens, scale=0.0):
+    """Paged GQA decode over the dequantised FP8 cache, the arithmetic of one
+    cpu_attention row (tests/test_attention.cu:66-97) per (sequence, query
+    head) in float64.  q: [B, Hq, D] (fp16 or fp32).  Returns float64 [B, Hq, D]."""
+    deq = dequant_fp8(pool_u8, g)[layer].astype(np.float64)  # [NP, Hkv, 2, P, D]
+    q = np.asarray(q).astype(np.float64)
+    B, Hq, D = q.shape
+    G = Hq // g.Hkv
+    sc = scale if scale > 0 else 1.0 / np.sqrt(D)
+    out = np.zeros((B, Hq, D))
+    for b in range(B):
+        n = int(seq_lens[b])
+        if n <= 0:
+            continue
+        pages = np.asarray(block_tables[b][: (n + g.P - 1) // g.P])
+        kv = deq[pages]  # [np, Hkv, 2, P, D]
+        K = kv[:, :, 0].transpose(1, 0, 2, 3).reshape(g.Hkv, -1, D)[:, :n]
+        V = kv[:, :, 1].transpose(1, 0, 2, 3).reshape(g.Hkv, -1, D)[:, :n]
+        for h in range(Hq):
+            s = K[h // G] @ q[b, h] * sc
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ V[h // G]
     return out

@@ -13,6 +13,8 @@
  *   - MemoryManager pages     cuda/memory.cu:73-191            (byte pages, swap)
  *   - cpu_rope                tests/test_kernels.cu:697-716    (rotary embedding,
  *                             applied to Q and K_new at src/transformer.cpp:114-128)
+ *   - group quantisation      docs/ADRs/003-quantization-format.md:11-18 (symmetric
+ *                             per-group fp32 scale; FP8 pages use it with e4m3)
  *
  * Floating point follows cpu_attention exactly: fp32 accumulation in the same
  * loop order, -FLT_MAX fill, max-subtracted expf, divide by the sum, then the
@@ -358,4 +360,145 @@ void or_rope(const float* in, float* out, int head_dim, int pos, float theta_bas
         out[2 * i] = x0 * cos_t - x1 * sin_t;
         out[2 * i + 1] = x0 * sin_t + x1 * cos_t;
     }
+}
+
+/* ---- FP8 KV pages ---------------------------------------------------------
+ * Restates the product's FP8 page format: the group-wise symmetric rule of
+ * VULCAN's ADR-003 (docs/ADRs/003-quantization-format.md:11-18: one fp32 scale
+ * per group, scale = max|group| / qmax, value = code * scale) with the OCP
+ * FP8 E4M3 element (qmax 448) and the group = one token's K or V row of one
+ * head.  Element codes follow the OCP 8-bit floating point definition: 1 sign,
+ * 4 exponent (bias 7), 3 mantissa bits, subnormals for exponent 0, no
+ * infinities, S.1111.111 = NaN, largest finite 448. */
+
+/* Nearest-even E4M3 code of x; finite values beyond 448 saturate to +-448. */
+uint8_t or_e4m3_encode(float x) {
+    const uint8_t sign = signbit(x) ? 0x80 : 0x00;
+    const float a = fabsf(x);
+    if (isnan(x)) return (uint8_t)(sign | 0x7F);
+    if (a >= 448.0f) return (uint8_t)(sign | 0x7E);
+    if (a < 0.015625f) { /* below 2^-6: subnormal steps of 2^-9 (code 8 is 2^-6) */
+        const float q = nearbyintf(a * 512.0f);
+        return (uint8_t)(sign | (uint8_t)q);
+    }
+    int e2;
+    const float f = frexpf(a, &e2); /* a = f * 2^e2, f in [0.5, 1) */
+    int E = e2 - 1;                 /* a = (2f) * 2^E, 2f in [1, 2) */
+    float m = nearbyintf((2.0f * f - 1.0f) * 8.0f);
+    if (m >= 8.0f) {
+        m = 0.0f;
+        ++E;
+    }
+    if (E > 8 || (E == 8 && m > 6.0f)) return (uint8_t)(sign | 0x7E);
+    return (uint8_t)(sign | (uint8_t)((E + 7) << 3) | (uint8_t)m);
+}
+
+float or_e4m3_decode(uint8_t c) {
+    const int E = (c >> 3) & 15, m = c & 7;
+    float v;
+    if (E == 15 && m == 7) v = NAN;
+    else if (E == 0) v = ldexpf((float)m, -9);
+    else v = ldexpf(1.0f + (float)m / 8.0f, E - 7);
+    return (c & 0x80) ? -v : v;
+}
+
+/* One group: amax below FLT_MIN gives scale 0 and zero codes; otherwise
+ * code_i = e4m3(x_i * (448 / amax)), scale = amax / 448 (fp32, each rounded once). */
+void or_fp8_quant_row(const float* x, int n, uint8_t* codes, float* scale) {
+    float a = 0.0f;
+    for (int i = 0; i < n; ++i)
+        if (fabsf(x[i]) > a) a = fabsf(x[i]);
+    if (!(a >= FLT_MIN)) {
+        *scale = 0.0f;
+        memset(codes, 0, (size_t)n);
+        return;
+    }
+    const float inv = 448.0f / a;
+    *scale = a / 448.0f;
+    for (int i = 0; i < n; ++i) codes[i] = or_e4m3_encode(x[i] * inv);
+}
+
+/* Byte offsets inside the block of one (layer, page, head), 2*16*D + 128 bytes:
+ * K codes [16][D] (16-byte chunks of token t's row rotated by XOR (t & 7)),
+ * V codes [D][16] (token order 0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15),
+ * 16 K scales, 16 V scales (fp32). */
+static inline int64_t or_fp8_k_off(int t, int d, int D) { return (int64_t)t * D + ((((d >> 4) ^ (t & 7))) << 4) + (d & 15); }
+static inline int or_fp8_v_pos(int t) { return ((t & 7) >> 1) * 4 + (t & 1) + ((t >> 3) << 1); }
+static inline int64_t or_fp8_v_off(int t, int d, int D, int P) { return (int64_t)P * D + (int64_t)d * P + or_fp8_v_pos(t); }
+static inline int64_t or_fp8_scale_off(int kv, int t, int D, int P) { return 2LL * P * D + (kv * P + t) * 4; }
+static inline int64_t or_fp8_block(int Hkv, int D, int P, int num_pages, int layer, int page, int h) {
+    return (((int64_t)layer * num_pages + page) * Hkv + h) * (2LL * P * D + 8LL * P);
+}
+
+/*
+ * KVCache::append (src/kv_cache.cpp:84-128) into an FP8 pool: token t of
+ * sequence b at pos = positions[b] + t, every KV head, K and V rows given in
+ * fp32 [B, T, Hkv, D] (fp16 inputs are widened exactly by the caller; a
+ * rotated K is rotated before).  Returns 0, or -1 when an entry was skipped.
+ */
+int or_append_fp8(uint8_t* pool, int L, int Hkv, int D, int P, int num_pages, int layer, const float* k,
+                  const float* v, const int32_t* block_tables, int bt_stride, const int32_t* positions, int B,
+                  int T) {
+    (void)L;
+    int bad = 0;
+    uint8_t* kc = (uint8_t*)malloc((size_t)D);
+    uint8_t* vc = (uint8_t*)malloc((size_t)D);
+    for (int b = 0; b < B; ++b)
+        for (int t = 0; t < T; ++t) {
+            const int pos = positions[b] + t;
+            if (pos < 0 || pos / P >= bt_stride) {
+                bad = 1;
+                continue;
+            }
+            const int32_t page = block_tables[(int64_t)b * bt_stride + pos / P];
+            if (page < 0 || page >= num_pages) {
+                bad = 1;
+                continue;
+            }
+            const int slot = pos % P;
+            for (int h = 0; h < Hkv; ++h) {
+                const int64_t src = (((int64_t)b * T + t) * Hkv + h) * D;
+                float ks, vs;
+                or_fp8_quant_row(k + src, D, kc, &ks);
+                or_fp8_quant_row(v + src, D, vc, &vs);
+                uint8_t* blk = pool + or_fp8_block(Hkv, D, P, num_pages, layer, page, h);
+                for (int d = 0; d < D; ++d) {
+                    blk[or_fp8_k_off(slot, d, D)] = kc[d];
+                    blk[or_fp8_v_off(slot, d, D, P)] = vc[d];
+                }
+                memcpy(blk + or_fp8_scale_off(0, slot, D, P), &ks, 4);
+                memcpy(blk + or_fp8_scale_off(1, slot, D, P), &vs, 4);
+            }
+        }
+    free(kc);
+    free(vc);
+    return bad ? -1 : 0;
+}
+
+/* Dequantised copy of an FP8 pool: out fp32 [L][num_pages][Hkv][2][P][D],
+ * value = code * scale. */
+void or_dequant_fp8(const uint8_t* pool, int L, int Hkv, int D, int P, int num_pages, float* out) {
+    for (int layer = 0; layer < L; ++layer)
+        for (int page = 0; page < num_pages; ++page)
+            for (int h = 0; h < Hkv; ++h) {
+                const uint8_t* blk = pool + or_fp8_block(Hkv, D, P, num_pages, layer, page, h);
+                float* o = out + (((int64_t)layer * num_pages + page) * Hkv + h) * 2LL * P * D;
+                for (int t = 0; t < P; ++t) {
+                    float ks, vs;
+                    memcpy(&ks, blk + or_fp8_scale_off(0, t, D, P), 4);
+                    memcpy(&vs, blk + or_fp8_scale_off(1, t, D, P), 4);
+                    for (int d = 0; d < D; ++d) {
+                        o[(int64_t)t * D + d] = or_e4m3_decode(blk[or_fp8_k_off(t, d, D)]) * ks;
+                        o[((int64_t)P + t) * D + d] = or_e4m3_decode(blk[or_fp8_v_off(t, d, D, P)]) * vs;
+                    }
+                }
+            }
+}
+
+void or_e4m3_encode_array(const float* x, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = or_e4m3_encode(x[i]);
+}
+
+void or_e4m3_decode_array(const uint8_t* c, float* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = or_e4m3_decode(c[i]);
 }

@@ -1,0 +1,195 @@
+"""GPU parity tests of FP8 (e4m3 + per-row fp32 scale) KV pages against the
+oracle's restatement (oracle/vk_oracle.c: or_append_fp8, or_dequant_fp8).
+
+Append, fused append and page copy are bit-exact against the oracle on the
+whole byte image of the pool (unwritten slots hold random bytes on both
+sides).  Decode outputs are compared with the oracle's float64 attention over
+the dequantised cache under the fp16 attention tolerance."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import assert_close_attn, dev_f16, dev_i32, random_layout
+
+pytestmark = pytest.mark.gpu
+THETA = 10000.0
+
+
+@pytest.fixture(scope="module")
+def vk(cuda_ok):
+    import vulcan_b200
+    vulcan_b200.load()
+    return vulcan_b200
+
+
+def fp8_pool(vk, g, rng):
+    """An FP8 pool whose bytes start random, and the same bytes on the host."""
+    pool = vk.PagedKVPool(g.L, g.Hkv, g.D, g.num_pages, kv_format="fp8")
+    host = rng.integers(0, 256, size=(g.L, g.num_pages, g.Hkv, pool.block_bytes), dtype=np.uint8)
+    pool.block_view().copy_(torch.from_numpy(host))
+    return pool, host
+
+
+def rows(rng, *shape, f32=False):
+    x = rng.standard_normal(shape).astype(np.float32) * 0.5
+    return x if f32 else x.astype(np.float16)
+
+
+def assert_bytes(pool, host, what):
+    got = pool.block_view().cpu().numpy()
+    bad = got != host
+    assert not bad.any(), "%s: %d bytes differ (first at %s)" % (what, int(bad.sum()), np.argwhere(bad)[0])
+
+
+@pytest.mark.parametrize("f32", [False, True])
+def test_fp8_append_bit_exact(vk, f32):
+    rng = np.random.default_rng(81 + f32)
+    B, T, Hkv, D, L = 3, 37, 2, 128, 2
+    pos = np.array([0, 5, 4000], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, pos + T)
+    pool, host = fp8_pool(vk, g, rng)
+    k, v = rows(rng, B, T, Hkv, D, f32=f32), rows(rng, B, T, Hkv, D, f32=f32)
+    k[0, 3, 1] = 0  # an all-zero row: scale 0, codes 0
+    k[1, 0, 0, 7] = 60.0  # one large element: the others quantise coarsely
+    pool.append(1, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), dev_i32(bt), dev_i32(pos))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert oracle.append_fp8(host, g, 1, k, v, bt, pos) == 0
+    assert_bytes(pool, host, "FP8 append (%s inputs)" % ("fp32" if f32 else "fp16"))
+
+
+def fill_history(vk, pool, host, g, rng, layer, bt, lens, rope=False):
+    """Appends tokens 0 .. len-2 of every sequence (GPU and oracle)."""
+    for b, n in enumerate(lens):
+        if n <= 1:
+            continue
+        k, v = rows(rng, 1, n - 1, g.Hkv, g.D), rows(rng, 1, n - 1, g.Hkv, g.D)
+        pool.append(layer, dev_f16(k), dev_f16(v), dev_i32(bt[b:b + 1]), dev_i32([0]))
+        kk = k.astype(np.float32)
+        if rope:
+            kk = np.stack([oracle.rope(kk[0, t], [t] * g.Hkv, THETA) for t in range(n - 1)])[None]
+        assert oracle.append_fp8(host, g, layer, kk, v, bt[b:b + 1], np.array([0], np.int32)) == 0
+
+
+@pytest.mark.parametrize("G", [8, 16])
+def test_fp8_planned_decode_fused_append(vk, G):
+    rng = np.random.default_rng(83 + G)
+    Hkv, D, L, layer = 2, 128, 2, 1
+    Hq = G * Hkv
+    lens = np.array([1, 15, 16, 17, 300, 2049, 8000], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool, host = fp8_pool(vk, g, rng)
+    fill_history(vk, pool, host, g, rng, layer, bt, lens)
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert_bytes(pool, host, "FP8 history append")
+    B = len(lens)
+    q = rows(rng, B, Hq, D)
+    kn, vn = rows(rng, B, Hkv, D), rows(rng, B, Hkv, D)
+    out = pool.plan(lens.tolist(), Hq).run(layer, dev_f16(q), dev_i32(bt), k_new=dev_f16(kn), v_new=dev_f16(vn))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert oracle.append_fp8(host, g, layer, kn[:, None], vn[:, None], bt, lens - 1) == 0
+    assert_bytes(pool, host, "FP8 pool after the fused append")
+    ref = oracle.decode_fp8(host, g, layer, q, bt, lens)
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 planned decode G=%d" % G)
+
+
+def test_fp8_decode_small_v_rows(vk):
+    """V rows of very different magnitudes (1e-4 .. 10) in one page: the per-page
+    power-of-two normalisation of the V scales keeps fp16 P in range."""
+    rng = np.random.default_rng(88)
+    Hkv, D, L, layer, G = 1, 128, 1, 0, 8
+    lens = np.array([16, 40, 333], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool, host = fp8_pool(vk, g, rng)
+    for b, n in enumerate(lens):
+        k = rows(rng, 1, n, Hkv, D, f32=True)
+        v = rows(rng, 1, n, Hkv, D, f32=True) * (10.0 ** rng.uniform(-4, 1, size=(1, n, 1, 1))).astype(np.float32)
+        pool.append(layer, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(), dev_i32(bt[b:b + 1]),
+                    dev_i32([0]))
+        assert oracle.append_fp8(host, g, layer, k, v, bt[b:b + 1], np.array([0], np.int32)) == 0
+    q = rows(rng, len(lens), G * Hkv, D)
+    out = pool.plan(lens.tolist(), G * Hkv).run(layer, dev_f16(q), dev_i32(bt))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert_bytes(pool, host, "FP8 append of scaled rows")
+    ref = oracle.decode_fp8(host, g, layer, q, bt, lens)
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 decode, V rows over 5 decades")
+
+
+def test_fp8_decode_rope(vk):
+    rng = np.random.default_rng(85)
+    Hkv, D, L, layer, G = 2, 128, 1, 0, 8
+    Hq = G * Hkv
+    lens = np.array([3, 40, 1000], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool, host = fp8_pool(vk, g, rng)
+    pool.set_rope(THETA)
+    fill_history(vk, pool, host, g, rng, layer, bt, lens, rope=True)
+    B = len(lens)
+    q = rows(rng, B, Hq, D)
+    kn, vn = rows(rng, B, Hkv, D), rows(rng, B, Hkv, D)
+    out = pool.plan(lens.tolist(), Hq).run(layer, dev_f16(q), dev_i32(bt), k_new=dev_f16(kn), v_new=dev_f16(vn))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    newpos = lens - 1
+    krot = np.stack([oracle.rope(kn[b].astype(np.float32), [newpos[b]] * Hkv, THETA) for b in range(B)])
+    qrot = np.stack([oracle.rope(q[b].astype(np.float32), [newpos[b]] * Hq, THETA) for b in range(B)])
+    assert oracle.append_fp8(host, g, layer, krot[:, None], vn[:, None], bt, newpos) == 0
+    # K codes may differ by one step where the device's sin/cos differ from the
+    # host's by an ulp; the attention output is held to the usual tolerance
+    got = pool.block_view().cpu().numpy()
+    ref = oracle.decode_fp8(host, g, layer, qrot.astype(np.float16), bt, lens)
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 planned decode with RoPE")
+    dg = oracle.dequant_fp8(got, g)
+    dh = oracle.dequant_fp8(host, g)
+    for b, n in enumerate(lens):
+        pages = bt[b, :(n + 15) // 16]
+        a = dg[layer, pages].transpose(1, 2, 0, 3, 4).reshape(Hkv, 2, -1, D)[:, :, :n]
+        h = dh[layer, pages].transpose(1, 2, 0, 3, 4).reshape(Hkv, 2, -1, D)[:, :, :n]
+        assert np.array_equal(a[:, 1], h[:, 1]), "V rows"
+        step = np.abs(h[:, 0]).max(axis=-1, keepdims=True) * (32.0 / 448.0)  # largest e4m3 step (416 -> 448)
+        assert (np.abs(a[:, 0] - h[:, 0]) <= 1.01 * step + 1e-6).all(), "K rows with RoPE"
+
+
+def test_fp8_copy_and_swap(vk):
+    rng = np.random.default_rng(86)
+    g = oracle.Geom(3, 2, 128, 16, 12)
+    pool, host = fp8_pool(vk, g, rng)
+    src, dst = np.array([1, 4, 7], np.int32), np.array([9, 2, 11], np.int32)
+    pool.copy_pages(dev_i32(src), dev_i32(dst))
+    torch.cuda.synchronize()
+    seg = g.Hkv * pool.block_bytes
+    oracle.copy_pages(host.reshape(-1), g.L, seg, seg * g.num_pages, g.num_pages, src, dst)
+    assert_bytes(pool, host, "FP8 page copy")
+    ids = pool.alloc(4)
+    pinned = torch.empty(4 * pool.page_bytes, dtype=torch.uint8).pin_memory()
+    before = pool.block_view().cpu().numpy().copy()
+    pool.swap_out(ids, pinned)
+    pool.block_view().zero_()
+    pool.swap_in_to(pinned, ids)
+    torch.cuda.synchronize()
+    after = pool.block_view().cpu().numpy()
+    assert np.array_equal(after[:, ids], before[:, ids]), "FP8 swap round trip"
+
+
+def test_fp8_unsupported_entry_points(vk):
+    rng = np.random.default_rng(87)
+    g = oracle.Geom(1, 1, 128, 16, 4)
+    pool, _ = fp8_pool(vk, g, rng)
+    q = dev_f16(rows(rng, 1, 8, 128))
+    bt = dev_i32([[0, 1]])
+    with pytest.raises(vk.VKError):
+        pool.decode(0, q, bt, dev_i32([20]), 20)
+    with pytest.raises(vk.VKError):
+        pool.prefill(0, dev_f16(rows(rng, 1, 4, 8, 128)), bt, dev_i32([0]))
+    with pytest.raises(RuntimeError):
+        pool.kv_view()
+    with pytest.raises(vk.VKError):
+        vk.PagedKVPool(1, 1, 64, 4, kv_format="fp8")

@@ -4,6 +4,7 @@ allocator tests.  No GPU needed."""
 import os
 
 import numpy as np
+import torch
 import pytest
 
 import oracle
@@ -236,3 +237,73 @@ def test_oracle_rope_properties():
     n_in = np.hypot(x[0::2], x[1::2])
     n_out = np.hypot(y[0::2], y[1::2])
     assert np.abs(n_in - n_out).max() < 1e-4
+
+
+# ---------------------------------------------------------------- FP8 pages
+
+def test_e4m3_encoder_matches_torch():
+    """The oracle's E4M3 encoder (nearest even) and decoder agree with torch's
+    float8_e4m3fn on every code and on in-range values including ties."""
+    rng = np.random.default_rng(90)
+    steps = oracle.e4m3_decode(np.arange(256, dtype=np.uint8))
+    fin = np.isfinite(steps)
+    vals = np.unique(steps[fin]).astype(np.float32)
+    mids = ((vals[:-1] + vals[1:]) / 2).astype(np.float32)  # ties between neighbouring codes
+    x = np.concatenate([vals, mids,
+                        (rng.standard_normal(50000) * 40).astype(np.float32),
+                        np.float32(2.0) ** rng.integers(-12, 9, 5000).astype(np.float32),
+                        np.array([0.0, -0.0, 2 ** -10, 3 * 2 ** -11, 1e-30], np.float32)])
+    x = x[np.abs(x) <= 448]
+    want = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(oracle.e4m3_encode(x), want)
+    td = torch.from_numpy(np.arange(256, dtype=np.uint8)).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(np.isnan(steps), np.isnan(td))
+    assert np.array_equal(steps[fin], td[fin])
+    # saturation: finite values past 448 clamp to +-448 (code 0x7E / 0xFE)
+    assert list(oracle.e4m3_encode(np.array([449, 464, 470, 1e9, -500], np.float32))) == [0x7E] * 4 + [0xFE]
+
+
+def test_fp8_group_rule():
+    """ADR-003's symmetric group rule with qmax 448: the largest element maps to
+    +-448, every element is within half a step of code * scale, zero rows give
+    scale 0."""
+    rng = np.random.default_rng(91)
+    for _ in range(50):
+        x = (rng.standard_normal(128) * rng.uniform(0.01, 10)).astype(np.float32)
+        codes, scale = oracle.fp8_quant_row(x)
+        assert scale == np.float32(np.abs(x).max()) / np.float32(448.0)
+        deq = oracle.e4m3_decode(codes).astype(np.float64) * scale
+        i = np.argmax(np.abs(x))
+        assert abs(oracle.e4m3_decode(codes[i:i + 1])[0]) == 448.0
+        y = np.abs(x.astype(np.float64)) / scale
+        half = np.where(y < 2 ** -6, 2.0 ** -10, 2.0 ** (np.floor(np.log2(np.maximum(y, 2 ** -6))) - 4))
+        assert (np.abs(deq - x) <= half * scale * 1.0001 + 1e-12).all()
+    codes, scale = oracle.fp8_quant_row(np.zeros(128, np.float32))
+    assert scale == 0 and not codes.any()
+
+
+def test_fp8_append_dequant_round_trip():
+    """Append then dequantise returns code * scale at each token's slot for K and V
+    (the block layout functions are mutually consistent) and leaves other slots."""
+    rng = np.random.default_rng(92)
+    g = oracle.Geom(2, 2, 128, 16, 6)
+    bb = oracle.fp8_block_bytes(128)
+    pool = rng.integers(0, 256, size=(g.L, g.num_pages, g.Hkv, bb), dtype=np.uint8)
+    before = pool.copy()
+    bt = np.array([[3, 1, 4]], np.int32)
+    T = 20
+    k = (rng.standard_normal((1, T, 2, 128)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((1, T, 2, 128)) * 0.5).astype(np.float32)
+    assert oracle.append_fp8(pool, g, 1, k, v, bt, np.array([9], np.int32)) == 0
+    deq = oracle.dequant_fp8(pool, g)
+    for t in range(T):
+        pos = 9 + t
+        page, slot = bt[0, pos // 16], pos % 16
+        for h in range(2):
+            for kv, x in ((0, k), (1, v)):
+                codes, scale = oracle.fp8_quant_row(x[0, t, h])
+                want = oracle.e4m3_decode(codes) * scale
+                assert np.array_equal(deq[1, page, h, kv, slot], want)
+    untouched = [p for p in range(g.num_pages) if p not in (3, 1)]
+    assert np.array_equal(pool[:, untouched], before[:, untouched])
+    assert np.array_equal(pool[0], before[0])

@@ -37,6 +37,8 @@ SIGNATURES = {
     "vk_pool_destroy": (c_i32, [vp]),
     "vk_pool_base": (vp, [vp]),
     "vk_pool_page_bytes": (c_u64, [vp]),
+    "vk_pool_create_fmt": (c_i32, [ctypes.POINTER(VkPoolCfg), c_i32, vp, c_sz, ctypes.POINTER(vp)]),
+    "vk_pool_kv_format": (c_i32, [vp]),
     "vk_pool_num_pages": (c_i32, [vp]),
     "vk_pool_check": (c_i32, [vp, u32p]),
     "vk_alloc_pages": (c_i32, [vp, c_i32, i32p]),

@@ -8,6 +8,7 @@
 // one launch moves every row with 16-byte vector loads and stores, one warp per
 // (token, kv head) covering its K row and V row.
 #include "vk_internal.h"
+#include "vk_fp8.cuh"
 #include "vk_ptx.cuh"
 #include "vk_rope.cuh"
 
@@ -116,6 +117,93 @@ vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, 
         append_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "append_kernel launch");
+}
+
+// ---------------------------------------------------------------- K1 on FP8 pools
+
+// One warp per (token, kv head): the K row (rotated first when RoPE is on) and
+// the V row are quantised in fp32 (vk_fp8.cuh) from the fp16 or fp32 inputs and
+// written as codes and scales into the token's slot of its page block.
+template <bool F32>
+__global__ void __launch_bounds__(256) append_fp8_kernel(const AppendParams p) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.Hkv;
+    if (row >= rows) return;
+    const int h = static_cast<int>(row % p.Hkv);
+    const int64_t bt_idx = row / p.Hkv;
+    const int t = static_cast<int>(bt_idx % p.T);
+    const int b = static_cast<int>(bt_idx / p.T);
+    const int pos = p.pos[b] + t;
+    if (pos < 0 || pos / p.P >= p.bt_stride) {
+        if (lane == 0) atomicOr(p.err, VK_ERR_TABLE_INDEX);
+        return;
+    }
+    const int32_t page = p.bt[static_cast<int64_t>(b) * p.bt_stride + pos / p.P];
+    if (page < 0 || page >= p.num_pages) {
+        if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
+        return;
+    }
+    const int64_t src = row * kFp8Dim + 4 * lane;
+    float xk[4], xv[4];
+    if constexpr (F32) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.k) + src));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.v) + src));
+        xk[0] = a.x; xk[1] = a.y; xk[2] = a.z; xk[3] = a.w;
+        xv[0] = c.x; xv[1] = c.y; xv[2] = c.z; xv[3] = c.w;
+    } else {
+        const uint2 kw = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(p.k) + src));
+        const uint2 vw = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(p.v) + src));
+        float2 f;
+        f = __half22float2(*reinterpret_cast<const __half2*>(&kw.x)); xk[0] = f.x; xk[1] = f.y;
+        f = __half22float2(*reinterpret_cast<const __half2*>(&kw.y)); xk[2] = f.x; xk[3] = f.y;
+        f = __half22float2(*reinterpret_cast<const __half2*>(&vw.x)); xv[0] = f.x; xv[1] = f.y;
+        f = __half22float2(*reinterpret_cast<const __half2*>(&vw.y)); xv[2] = f.x; xv[3] = f.y;
+    }
+    if (p.rope_freq != nullptr) {
+        float2 f;
+        f = rope_pair(xk[0], xk[1], 2 * lane, pos, p.rope_freq); xk[0] = f.x; xk[1] = f.y;
+        f = rope_pair(xk[2], xk[3], 2 * lane + 1, pos, p.rope_freq); xk[2] = f.x; xk[3] = f.y;
+    }
+    float ks, vs;
+    const uint32_t kc = fp8_quant_row(xk, ks);
+    const uint32_t vc = fp8_quant_row(xv, vs);
+    char* blk = p.base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes + static_cast<uint64_t>(h) * p.head_bytes;
+    fp8_store_token(blk, pos % p.P, lane, kc, vc, ks, vs);
+}
+
+vk_status launch_append_fp8(vk_pool* pool, int layer, const void* k, const void* v, bool f32,
+                            const int32_t* bt, int bt_stride, const int32_t* pos, int B, int T,
+                            cudaStream_t st) {
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16)
+        return fail(VK_INVALID_ARG, "k_new/v_new must be 16-byte aligned");
+    AppendParams p;
+    p.base = pool->base;
+    p.k = k;
+    p.v = v;
+    p.bt = bt;
+    p.pos = pos;
+    p.err = pool->d_err;
+    p.seg_bytes = pool->seg_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
+    p.head_bytes = pool->head_bytes;
+    p.bt_stride = bt_stride;
+    p.B = B;
+    p.T = T;
+    p.Hkv = pool->cfg.num_kv_heads;
+    p.D = pool->cfg.head_dim;
+    p.P = pool->cfg.page_tokens;
+    p.num_pages = pool->num_pages;
+    p.rope_freq = pool->rope_freq;
+    const int64_t threads = static_cast<int64_t>(B) * T * p.Hkv * 32;
+    const int64_t blocks = (threads + 255) / 256;
+    if (blocks > 0x7fffffff) return fail(VK_INVALID_ARG, "append too large for one launch");
+    if (f32)
+        append_fp8_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+    else
+        append_fp8_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? VK_OK : cuda_fail(e, "append_fp8_kernel launch");
 }
 
 // ---------------------------------------------------------------- K4 copy

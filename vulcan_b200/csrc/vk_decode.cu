@@ -407,6 +407,8 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
                     void* workspace, size_t workspace_bytes, void* stream) {
     if (!pool) return fail(VK_INVALID_ARG, "pool is NULL");
     if (!pool->kv) return fail(VK_UNSUPPORTED, "decode needs a KV pool (page_bytes == 0)");
+    if (pool->kv_format != VK_KV_FP16)
+        return fail(VK_UNSUPPORTED, "vk_decode reads fp16 pages; FP8 pools decode through vk_decode_run");
     if (!pool->tmap_ok) return fail(VK_UNSUPPORTED, "pool too large for 32-bit TMA row coordinates");
     if (pool->cfg.page_tokens != kPageTokens) return fail(VK_UNSUPPORTED, "decode supports page_tokens == 16");
     const int D = pool->cfg.head_dim, Hkv = pool->cfg.num_kv_heads;

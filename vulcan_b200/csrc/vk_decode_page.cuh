@@ -22,8 +22,10 @@ struct WarpSoftmaxState {
     float m[NT][2];
     float l[NT][2];
     float acc[NT][D / 16][4];
+    float vf;  // FP8 pages: acc holds the true sums divided by vf (a power of two)
 
     __device__ __forceinline__ void reset() {
+        vf = 1.f;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             m[nt][0] = m[nt][1] = -INFINITY;

@@ -38,10 +38,14 @@
 //    ranks' flags of the previous layer's slot.
 //  * RoPE fused (optional): q and the new K rows are rotated in registers as
 //    they are loaded (vk_rope.cuh).
+//  * FP8 pools (FMT = 1, vk_fp8.cuh): a page block (codes and scales, 4,224
+//    bytes at D=128) arrives in one bulk copy; the appended token is quantised
+//    by the consuming warp, stored to the pool and patched into the stage.
 #include <algorithm>
 #include <vector>
 
 #include "vk_decode_page.cuh"
+#include "vk_fp8.cuh"
 #include "vk_gather.cuh"
 #include "vk_internal.h"
 
@@ -89,9 +93,15 @@ struct PlanParams {
     int out_own;     // out is this rank's own slice (skip the local copy)
 };
 
-template <int D>
+// bytes of one stage: the K and V rows of one (page, head), fp16 or FP8 block
+template <int D, int FMT>
+__host__ __device__ constexpr int plan_stage_bytes() {
+    return FMT ? fp8_head_bytes(D) : 2 * kPageTokens * D * 2;
+}
+
+template <int D, int FMT>
 __host__ __device__ constexpr int plan_smem_bytes() {
-    return kPlanWarps * kPlanStages * (2 * kPageTokens * D * 2) + kPlanWarps * kPlanStages * 8 + 1024;
+    return kPlanWarps * kPlanStages * plan_stage_bytes<D, FMT>() + kPlanWarps * kPlanStages * 8 + 1024;
 }
 
 // Programmatic dependent launch: let the next kernel on the stream start
@@ -312,11 +322,11 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
     }
 }
 
-template <int D, int NT>
+template <int D, int NT, int FMT>
 __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                          const PlanParams p) {
     constexpr int P = kPageTokens;
-    constexpr int SB = 2 * P * D * 2;
+    constexpr int SB = plan_stage_bytes<D, FMT>();
     constexpr int NB = D / 64;
     constexpr int KS = D / 16;
     constexpr int NS = kPlanStages;
@@ -354,7 +364,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
 
     uint8_t* my_stages = smem + warp * NS * SB;
     uint64_t* full = bars + warp * NS;
-    if (lane == 0) prefetch_tmap(&tmap);
+    if (FMT == 0 && lane == 0) prefetch_tmap(&tmap);
     const uint64_t pol = l2_evict_first_policy();
 
     const int u0 = p.wfu[w];
@@ -405,12 +415,18 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             bad_stages |= 1u << s;
         }
         if (lane == 0) {
-            const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
             const uint32_t bar = smem_u32(&full[s]);
             mbar_expect_tx(bar, SB);
             const uint32_t dst = smem_u32(my_stages + s * SB);
+            if constexpr (FMT == 1) {
+                bulk_load(dst, p.pool_base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
+                                   static_cast<uint64_t>(hkv) * p.head_bytes,
+                          SB, bar, pol);
+            } else {
+                const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
 #pragma unroll
-            for (int hb = 0; hb < NB; ++hb) tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+                for (int hb = 0; hb < NB; ++hb) tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+            }
         }
         pf.next(p.uoff);
     };
@@ -429,8 +445,17 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
 
     uint32_t qf[NT][KS][2];
     WarpSoftmaxState<D, NT> st;
-    load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D, p.G, lane);
-    rope_q_frags<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
+    auto load_q = [&]() {
+        const __half* qs = p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D;
+        if constexpr (FMT == 1) {
+            load_q_frags_fp8<D, NT>(qf, qs, p.G, lane);
+            rope_q_frags_fp8<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
+        } else {
+            load_q_frags<D, NT>(qf, qs, p.G, lane);
+            rope_q_frags<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
+        }
+    };
+    load_q();
     st.reset();
 
     for (int j = 0; j < n; ++j) {
@@ -442,7 +467,29 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
         constexpr int NCH = D / 8;  // 16-byte chunks per row
         uint4 row_val[(2 * NCH + 31) / 32];
         int app_page = 0, app_slot = 0;
-        if (app) {
+        uint32_t q8k = 0u, q8v = 0u;  // FP8: the lane's codes of the new K and V rows
+        float q8ks = 0.f, q8vs = 0.f;
+        if (FMT == 1 && app) {
+            const int b = cu.u / p.Hkv, hkv = cu.u % p.Hkv;
+            app_page = p.bt[static_cast<int64_t>(b) * p.bt_stride + cu.p];
+            const int pos = p.ulen[cu.u] - 1;
+            app_slot = pos % P;
+            const int64_t src = (static_cast<int64_t>(b) * p.Hkv + hkv) * D + 4 * lane;
+            const uint2 kw = __ldg(reinterpret_cast<const uint2*>(p.k_new + src));
+            const uint2 vw = __ldg(reinterpret_cast<const uint2*>(p.v_new + src));
+            float xk[4], xv[4];
+            float2 f;
+            f = __half22float2(*reinterpret_cast<const __half2*>(&kw.x)); xk[0] = f.x; xk[1] = f.y;
+            f = __half22float2(*reinterpret_cast<const __half2*>(&kw.y)); xk[2] = f.x; xk[3] = f.y;
+            f = __half22float2(*reinterpret_cast<const __half2*>(&vw.x)); xv[0] = f.x; xv[1] = f.y;
+            f = __half22float2(*reinterpret_cast<const __half2*>(&vw.y)); xv[2] = f.x; xv[3] = f.y;
+            if (p.rope_freq != nullptr) {
+                f = rope_pair(xk[0], xk[1], 2 * lane, pos, p.rope_freq); xk[0] = f.x; xk[1] = f.y;
+                f = rope_pair(xk[2], xk[3], 2 * lane + 1, pos, p.rope_freq); xk[2] = f.x; xk[3] = f.y;
+            }
+            q8k = fp8_quant_row(xk, q8ks);
+            q8v = fp8_quant_row(xv, q8vs);
+        } else if (app) {
             const int b = cu.u / p.Hkv, hkv = cu.u % p.Hkv;
             app_page = p.bt[static_cast<int64_t>(b) * p.bt_stride + cu.p];
             app_slot = (p.ulen[cu.u] - 1) % P;
@@ -459,7 +506,13 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             }
         }
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&full[s]), (j / NS) & 1, p.err))) return;
-        if (app) {
+        if (FMT == 1 && app) {
+            char* blk = p.pool_base + p.layer_off + static_cast<uint64_t>(app_page) * p.seg_bytes +
+                        static_cast<uint64_t>(cu.u % p.Hkv) * p.head_bytes;
+            fp8_store_token(blk, app_slot, lane, q8k, q8v, q8ks, q8vs);
+            fp8_store_token(reinterpret_cast<char*>(my_stages + s * SB), app_slot, lane, q8k, q8v, q8ks, q8vs);
+            __syncwarp();
+        } else if (app) {
             const int hkv = cu.u % p.Hkv;
             char* dk = p.pool_base + p.layer_off + static_cast<uint64_t>(app_page) * p.seg_bytes +
                        static_cast<uint64_t>(hkv) * p.head_bytes + static_cast<uint64_t>(app_slot) * D * 2;
@@ -481,7 +534,8 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             __syncwarp();
         }
         const int valid = min(P, p.ulen[cu.u] - cu.p * P);
-        page_update<D, NT>(smem_u32(my_stages + s * SB), valid, qf, st, p.scale_log2, lane);
+        if constexpr (FMT == 1) page_update_fp8<D, NT>(smem_u32(my_stages + s * SB), valid, qf, st, p.scale_log2, lane);
+        else page_update<D, NT>(smem_u32(my_stages + s * SB), valid, qf, st, p.scale_log2, lane);
         // Every lane's ldmatrix results for stage s have been consumed by its MMAs
         // before __syncwarp returns, so the stage can be refilled.
         __syncwarp();
@@ -499,7 +553,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const int h0 = nt * 8 + (lane & 3) * 2;
-                    const float i0 = 1.f / st.l[nt][0], i1 = 1.f / st.l[nt][1];
+                    const float i0 = (FMT ? st.vf : 1.f) / st.l[nt][0], i1 = (FMT ? st.vf : 1.f) / st.l[nt][1];
 #pragma unroll
                     for (int mt = 0; mt < KS; ++mt) {
                         const int d = mt * 16 + (lane >> 2);
@@ -520,7 +574,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const int h0 = nt * 8 + (lane & 3) * 2;
-                    const float i0 = 1.f / st.l[nt][0], i1 = 1.f / st.l[nt][1];
+                    const float i0 = (FMT ? st.vf : 1.f) / st.l[nt][0], i1 = (FMT ? st.vf : 1.f) / st.l[nt][1];
 #pragma unroll
                     for (int mt = 0; mt < KS; ++mt) {
                         const int d = mt * 16 + (lane >> 2);
@@ -559,9 +613,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             }
             if (j + 1 < n) {
                 cu.next(p.uoff);
-                load_q_frags<D, NT>(qf, p.q + (static_cast<int64_t>(cu.u / p.Hkv) * p.Hq + (cu.u % p.Hkv) * p.G) * D,
-                                    p.G, lane);
-                rope_q_frags<D, NT>(qf, p.ulen[cu.u] - 1, p.rope_freq, lane);
+                load_q();
                 st.reset();
             }
         } else {
@@ -582,17 +634,17 @@ __global__ void plan_gather_wait_kernel(const GatherView g, int slot, const uint
     }
 }
 
-template <int D, int NT>
+template <int D, int NT, int FMT>
 static int plan_occupancy(int device, int* occ_out) {
     static int cache[64] = {};
     if (device < 0 || device >= 64) return -1;
     if (cache[device] == 0) {
-        constexpr int smem = plan_smem_bytes<D>();
-        if (cudaFuncSetAttribute(planned_decode_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        constexpr int smem = plan_smem_bytes<D, FMT>();
+        if (cudaFuncSetAttribute(planned_decode_kernel<D, NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return -1;
         int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, planned_decode_kernel<D, NT>, kPlanWarps * 32, smem) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, planned_decode_kernel<D, NT, FMT>, kPlanWarps * 32, smem) !=
                 cudaSuccess ||
             occ <= 0)
             return -1;
@@ -602,10 +654,12 @@ static int plan_occupancy(int device, int* occ_out) {
     return 0;
 }
 
-static int occupancy_for(int D, int NT, int device, int* occ) {
-    if (D == 128) return NT == 1 ? plan_occupancy<128, 1>(device, occ) : plan_occupancy<128, 2>(device, occ);
-    if (D == 64) return NT == 1 ? plan_occupancy<64, 1>(device, occ) : plan_occupancy<64, 2>(device, occ);
-    return NT == 1 ? plan_occupancy<256, 1>(device, occ) : plan_occupancy<256, 2>(device, occ);
+static int occupancy_for(int D, int NT, int fmt, int device, int* occ) {
+    if (fmt == VK_KV_FP8)  // FP8 pools: head_dim 128 only
+        return NT == 1 ? plan_occupancy<128, 1, 1>(device, occ) : plan_occupancy<128, 2, 1>(device, occ);
+    if (D == 128) return NT == 1 ? plan_occupancy<128, 1, 0>(device, occ) : plan_occupancy<128, 2, 0>(device, occ);
+    if (D == 64) return NT == 1 ? plan_occupancy<64, 1, 0>(device, occ) : plan_occupancy<64, 2, 0>(device, occ);
+    return NT == 1 ? plan_occupancy<256, 1, 0>(device, occ) : plan_occupancy<256, 2, 0>(device, occ);
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -613,7 +667,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace vk
 
 struct vk_decode_plan {
-    int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1;
+    int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1, fmt = VK_KV_FP16;
     int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
     mutable std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
@@ -650,6 +704,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     pl->G = G;
     pl->D = D;
     pl->NT = G <= 8 ? 1 : 2;
+    pl->fmt = pool->kv_format;
     const int U = batch * Hkv;
     pl->U = U;
     std::vector<int64_t> uoff(static_cast<size_t>(U) + 1, 0);
@@ -678,7 +733,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     int occ = 1;
     {
         DeviceGuard g(pool->device);
-        if (occupancy_for(D, pl->NT, pool->device, &occ) != 0) {
+        if (occupancy_for(D, pl->NT, pl->fmt, pool->device, &occ) != 0) {
             delete pl;
             return fail(VK_CUDA_ERROR, "occupancy query for the planned decode kernel failed");
         }
@@ -877,9 +932,11 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
                         const int32_t* block_tables, int32_t bt_stride, const void* k_new, const void* v_new,
                         float scale, void* workspace, void* stream) {
     if (!pool || !plan) return fail(VK_INVALID_ARG, "pool or plan is NULL");
-    if (!pool->kv || !pool->tmap_ok) return fail(VK_UNSUPPORTED, "decode needs a KV pool addressable by TMA");
-    if (pool->cfg.head_dim != plan->D || pool->cfg.num_kv_heads != plan->Hkv || pool->device != plan->device)
-        return fail(VK_INVALID_ARG, "plan was made for another pool shape or device");
+    if (!pool->kv || (pool->kv_format == VK_KV_FP16 && !pool->tmap_ok))
+        return fail(VK_UNSUPPORTED, "decode needs a KV pool addressable by TMA");
+    if (pool->cfg.head_dim != plan->D || pool->cfg.num_kv_heads != plan->Hkv || pool->device != plan->device ||
+        pool->kv_format != plan->fmt)
+        return fail(VK_INVALID_ARG, "plan was made for another pool shape, format or device");
     if (layer < 0 || layer >= pool->cfg.num_layers) return fail(VK_INVALID_ARG, "layer out of range");
     if (plan->B == 0) return VK_OK;
     GatherView gv{};
@@ -955,7 +1012,7 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
     int occ = 0;
-    if (occupancy_for(D, plan->NT, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
+    if (occupancy_for(D, plan->NT, plan->fmt, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
     const dim3 grid(plan->grid), block(kPlanWarps * 32);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -967,14 +1024,15 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t le = cudaSuccess;
-#define VK_LAUNCH(DD, NN)                                                                   \
+#define VK_LAUNCH(DD, NN, FF)                                                               \
     do {                                                                                    \
-        cfg.dynamicSmemBytes = plan_smem_bytes<DD>();                                       \
-        le = cudaLaunchKernelEx(&cfg, planned_decode_kernel<DD, NN>, pool->tmap, p);        \
+        cfg.dynamicSmemBytes = plan_smem_bytes<DD, FF>();                                   \
+        le = cudaLaunchKernelEx(&cfg, planned_decode_kernel<DD, NN, FF>, pool->tmap, p);    \
     } while (0)
-    if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1); else VK_LAUNCH(128, 2); }
-    else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1); else VK_LAUNCH(64, 2); }
-    else { if (plan->NT == 1) VK_LAUNCH(256, 1); else VK_LAUNCH(256, 2); }
+    if (plan->fmt == VK_KV_FP8) { if (plan->NT == 1) VK_LAUNCH(128, 1, 1); else VK_LAUNCH(128, 2, 1); }
+    else if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1, 0); else VK_LAUNCH(128, 2, 0); }
+    else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1, 0); else VK_LAUNCH(64, 2, 0); }
+    else { if (plan->NT == 1) VK_LAUNCH(256, 1, 0); else VK_LAUNCH(256, 2, 0); }
 #undef VK_LAUNCH
     if (le != cudaSuccess) return cuda_fail(le, "planned_decode_kernel launch");
     cudaError_t e = cudaGetLastError();

@@ -50,6 +50,7 @@ struct vk_pool {
     alignas(64) CUtensorMap tmap;    // 2-D view: rows of head_dim fp16, boxes of 64 x 32 rows (K+V)
     alignas(64) CUtensorMap tmap16;  // same view, boxes of 64 x 16 rows (K or V of one page)
     bool tmap_ok = false;
+    int32_t kv_format = VK_KV_FP16;  // page format of a KV pool (VK_KV_FP16 / VK_KV_FP8)
     int32_t prefill_path = 0;        // 0 auto, 1 mma.sync kernel, 2 tcgen05 kernel
     int32_t split_override = 0;
     int32_t plan_workers = 0;        // cap on planned-decode workers (0 = resident warps)
@@ -82,6 +83,9 @@ struct DeviceGuard {
 vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, bool f32,
                         const int32_t* bt, int bt_stride, const int32_t* pos, int B, int T,
                         cudaStream_t st);
+vk_status launch_append_fp8(vk_pool* pool, int layer, const void* k, const void* v, bool f32,
+                            const int32_t* bt, int bt_stride, const int32_t* pos, int B, int T,
+                            cudaStream_t st);
 vk_status launch_copy_pages(vk_pool* pool, const int32_t* src, const int32_t* dst, int n,
                             cudaStream_t st);
 vk_status launch_remap(int32_t* bt, int64_t entries, const int32_t* map, int map_len,

@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "vk_internal.h"
+#include "vk_fp8.cuh"
 
 namespace vk {
 
@@ -123,10 +124,18 @@ static vk_status make_tmap(vk_pool* p) {
     return VK_OK;
 }
 
-static vk_status check_cfg(const vk_pool_cfg* c, bool* kv, uint64_t* page_bytes) {
+// bytes of the K and V rows of one (layer, page, head)
+static uint64_t kv_head_bytes(const vk_pool_cfg* c, int fmt) {
+    if (fmt == VK_KV_FP8) return static_cast<uint64_t>(fp8_head_bytes(c->head_dim));
+    return 2ull * c->page_tokens * c->head_dim * 2;
+}
+
+static vk_status check_cfg(const vk_pool_cfg* c, int fmt, bool* kv, uint64_t* page_bytes) {
     if (!c) return fail(VK_INVALID_ARG, "cfg is NULL");
     if (c->num_pages <= 0) return fail(VK_INVALID_ARG, "num_pages must be > 0");
+    if (fmt != VK_KV_FP16 && fmt != VK_KV_FP8) return fail(VK_INVALID_ARG, "unknown kv_format");
     if (c->page_bytes) {
+        if (fmt != VK_KV_FP16) return fail(VK_INVALID_ARG, "a byte-page pool (page_bytes != 0) has no KV format");
         *kv = false;
         *page_bytes = c->page_bytes;
         return VK_OK;
@@ -135,9 +144,10 @@ static vk_status check_cfg(const vk_pool_cfg* c, bool* kv, uint64_t* page_bytes)
         return fail(VK_INVALID_ARG, "num_layers, num_kv_heads, head_dim, page_tokens must be > 0");
     if (c->head_dim % 8)
         return fail(VK_INVALID_ARG, "head_dim must be a multiple of 8 (16-byte rows)");
+    if (fmt == VK_KV_FP8 && (c->head_dim != kFp8Dim || c->page_tokens != kPageTokens))
+        return fail(VK_UNSUPPORTED, "FP8 pages need head_dim 128 and page_tokens 16");
     *kv = true;
-    *page_bytes = static_cast<uint64_t>(c->num_layers) * c->num_kv_heads * 2 * c->page_tokens *
-                  c->head_dim * 2;
+    *page_bytes = static_cast<uint64_t>(c->num_layers) * c->num_kv_heads * kv_head_bytes(c, fmt);
     return VK_OK;
 }
 
@@ -146,7 +156,7 @@ static vk_status check_cfg(const vk_pool_cfg* c, bool* kv, uint64_t* page_bytes)
 // contiguous region of num_pages*seg_bytes.
 static void set_geometry(vk_pool* p) {
     if (p->kv) {
-        p->head_bytes = 2ull * p->cfg.page_tokens * p->cfg.head_dim * 2;
+        p->head_bytes = kv_head_bytes(&p->cfg, p->kv_format);
         p->seg_bytes = p->head_bytes * p->cfg.num_kv_heads;
         p->nseg = p->cfg.num_layers;
         p->seg_stride = p->seg_bytes * static_cast<uint64_t>(p->num_pages);
@@ -166,7 +176,7 @@ static vk_status finish_create(vk_pool* p, vk_pool** out) {
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device) == cudaSuccess &&
         sms > 0)
         p->num_sms = sms;
-    if (p->kv) {
+    if (p->kv && p->kv_format == VK_KV_FP16) {  // FP8 blocks are fetched with untiled bulk copies
         vk_status s = make_tmap(p);
         if (s != VK_OK) return s;
     }
@@ -181,17 +191,18 @@ using namespace vk;
 
 extern "C" {
 
-vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool) {
+static vk_status pool_create_owned(const vk_pool_cfg* cfg, int fmt, vk_pool** out_pool) {
     if (!out_pool) return fail(VK_INVALID_ARG, "out_pool is NULL");
     *out_pool = nullptr;
     bool kv = false;
     uint64_t pb = 0;
-    vk_status s = check_cfg(cfg, &kv, &pb);
+    vk_status s = check_cfg(cfg, fmt, &kv, &pb);
     if (s != VK_OK) return s;
     DeviceGuard g(cfg->device);
     auto* p = new vk_pool();
     p->cfg = *cfg;
     p->kv = kv;
+    p->kv_format = fmt;
     p->device = cfg->device;
     p->page_bytes = pb;
     p->num_pages = cfg->num_pages;
@@ -220,13 +231,13 @@ vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool) {
     return s;
 }
 
-vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t bytes,
-                            vk_pool** out_pool) {
+static vk_status pool_create_in(const vk_pool_cfg* cfg, int fmt, void* device_mem, size_t bytes,
+                                vk_pool** out_pool) {
     if (!out_pool) return fail(VK_INVALID_ARG, "out_pool is NULL");
     *out_pool = nullptr;
     bool kv = false;
     uint64_t pb = 0;
-    vk_status s = check_cfg(cfg, &kv, &pb);
+    vk_status s = check_cfg(cfg, fmt, &kv, &pb);
     if (s != VK_OK) return s;
     if (!device_mem || (reinterpret_cast<uintptr_t>(device_mem) & 255))
         return fail(VK_INVALID_ARG, "device_mem must be non-NULL and 256-byte aligned");
@@ -236,6 +247,7 @@ vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t byt
     auto* p = new vk_pool();
     p->cfg = *cfg;
     p->kv = kv;
+    p->kv_format = fmt;
     p->device = cfg->device;
     p->page_bytes = pb;
     p->num_pages = cfg->num_pages;
@@ -250,6 +262,26 @@ vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t byt
     }
     return s;
 }
+
+vk_status vk_pool_create(const vk_pool_cfg* cfg, vk_pool** out_pool) {
+    return pool_create_owned(cfg, VK_KV_FP16, out_pool);
+}
+
+vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t bytes, vk_pool** out_pool) {
+    return pool_create_in(cfg, VK_KV_FP16, device_mem, bytes, out_pool);
+}
+
+vk_status vk_pool_create_fmt(const vk_pool_cfg* cfg, int32_t kv_format, void* device_mem, size_t bytes,
+                             vk_pool** out_pool) {
+    if (cfg && cfg->page_bytes) {
+        if (out_pool) *out_pool = nullptr;
+        return fail(VK_INVALID_ARG, "vk_pool_create_fmt makes KV pools: page_bytes must be 0");
+    }
+    return device_mem ? pool_create_in(cfg, kv_format, device_mem, bytes, out_pool)
+                      : pool_create_owned(cfg, kv_format, out_pool);
+}
+
+int32_t vk_pool_kv_format(const vk_pool* pool) { return pool && pool->kv ? pool->kv_format : -1; }
 
 vk_status vk_pool_destroy(vk_pool* pool) {
     if (!pool) return VK_OK;
@@ -460,6 +492,8 @@ static vk_status append_common(vk_pool* pool, int32_t layer, const void* k, cons
     if (batch == 0 || tokens == 0) return VK_OK;
     if (!k || !v || !bt || !pos) return fail(VK_INVALID_ARG, "NULL array");
     DeviceGuard g(pool->device);
+    if (pool->kv_format == VK_KV_FP8)
+        return launch_append_fp8(pool, layer, k, v, f32, bt, bt_stride, pos, batch, tokens, as_stream(stream));
     return launch_append(pool, layer, k, v, f32, bt, bt_stride, pos, batch, tokens, as_stream(stream));
 }
 

@@ -287,6 +287,7 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
                                 const int32_t* positions, int32_t batch, int32_t tokens,
                                 int32_t num_q_heads, float scale, void* stream) {
     if (!pool) return fail(VK_INVALID_ARG, "pool is NULL");
+    if (pool->kv && pool->kv_format != VK_KV_FP16) return fail(VK_UNSUPPORTED, "prefill reads fp16 pages only");
     if (!pool->kv || !pool->tmap_ok) return fail(VK_UNSUPPORTED, "prefill needs a KV pool addressable by TMA");
     if (pool->cfg.page_tokens != kPageTokens) return fail(VK_UNSUPPORTED, "prefill supports page_tokens == 16");
     const int D = pool->cfg.head_dim, Hkv = pool->cfg.num_kv_heads;

@@ -31,6 +31,7 @@ from . import _lib
 from ._lib import VKError, check
 
 PAGE_TOKENS = 16
+KV_FORMATS = {"fp16": 0, "fp8": 1}  # page formats (VK_KV_FP16, VK_KV_FP8)
 
 
 def _stream(stream=None) -> int:
@@ -69,38 +70,55 @@ class PagedKVPool:
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_pages: int,
                  page_tokens: int = PAGE_TOKENS, device=None, own_memory: bool = False,
-                 page_bytes: int = 0, zero: bool = True):
+                 page_bytes: int = 0, zero: bool = True, kv_format: str = "fp16"):
         self._lib = _lib.load()
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                            (device.index if isinstance(device, torch.device) else int(device)))
         self.device = dev
         self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
         self.page_tokens, self.num_pages = page_tokens, num_pages
+        if kv_format not in KV_FORMATS:
+            raise ValueError("kv_format must be one of %s" % sorted(KV_FORMATS))
+        self.kv_format = kv_format
+        fmt = KV_FORMATS[kv_format]
         cfg = _lib.VkPoolCfg(num_layers, num_kv_heads, head_dim, page_tokens, num_pages, dev.index,
                              page_bytes)
         self.kv = page_bytes == 0
-        self.page_bytes = page_bytes if page_bytes else (
-            num_layers * num_kv_heads * 2 * page_tokens * head_dim * 2)
+        # bytes of one (layer, page, head) block: fp16 K and V rows, or FP8 codes + 32 fp32 scales
+        self.block_bytes = (2 * page_tokens * head_dim + 8 * page_tokens if kv_format == "fp8"
+                            else 2 * page_tokens * head_dim * 2)
+        self.page_bytes = page_bytes if page_bytes else num_layers * num_kv_heads * self.block_bytes
         handle = ctypes.c_void_p()
         self.storage = None
         with torch.cuda.device(dev):
             if own_memory:
-                check(self._lib.vk_pool_create(ctypes.byref(cfg), ctypes.byref(handle)), "vk_pool_create")
+                check(self._lib.vk_pool_create_fmt(ctypes.byref(cfg), fmt, None, 0, ctypes.byref(handle))
+                      if fmt else self._lib.vk_pool_create(ctypes.byref(cfg), ctypes.byref(handle)), "vk_pool_create")
             else:
                 nbytes = self.page_bytes * num_pages
                 self.storage = (torch.zeros if zero else torch.empty)(nbytes, dtype=torch.uint8, device=dev)
-                check(self._lib.vk_pool_create_in(ctypes.byref(cfg), _ptr(self.storage), nbytes,
-                                                  ctypes.byref(handle)), "vk_pool_create_in")
+                check(self._lib.vk_pool_create_fmt(ctypes.byref(cfg), fmt, _ptr(self.storage), nbytes,
+                                                   ctypes.byref(handle))
+                      if fmt else self._lib.vk_pool_create_in(ctypes.byref(cfg), _ptr(self.storage), nbytes,
+                                                              ctypes.byref(handle)), "vk_pool_create_in")
+        if self.kv and self._lib.vk_pool_kv_format(handle) != fmt:
+            raise RuntimeError("library reports another page format than requested")
         self.handle = handle
         self._ws = None
 
     # ------------------------------------------------------------------ views
     def kv_view(self) -> torch.Tensor:
         """fp16 view [L, num_pages, Hkv, 2, page_tokens, head_dim] of the pool."""
-        if self.storage is None or not self.kv:
-            raise RuntimeError("kv_view needs a torch-backed KV pool")
+        if self.storage is None or not self.kv or self.kv_format != "fp16":
+            raise RuntimeError("kv_view needs a torch-backed fp16 KV pool")
         return self.storage.view(torch.float16).view(self.num_layers, self.num_pages, self.num_kv_heads,
                                                      2, self.page_tokens, self.head_dim)
+
+    def block_view(self) -> torch.Tensor:
+        """uint8 view [L, num_pages, Hkv, block_bytes] of the pool (either format)."""
+        if self.storage is None or not self.kv:
+            raise RuntimeError("block_view needs a torch-backed KV pool")
+        return self.storage.view(self.num_layers, self.num_pages, self.num_kv_heads, self.block_bytes)
 
     @property
     def base_ptr(self) -> int:
