@@ -203,10 +203,11 @@ struct PageIt {
 // out = sum_k 2^(lse_k - m) o_k / sum_k 2^(lse_k - m), written as fp16, in one
 // streaming pass with a running max.  IT = float4 items per lane (items
 // f = lane + 32 i, i < IT, of the task's [hs, D] block); the loads of KB
-// pieces (partials and their lse) are issued together.
-template <int D, int NT, int IT>
+// pieces (partials and their lse) are issued together.  FP8 pools (FMT 1)
+// batch fewer pieces: the kernel then runs 6 CTAs per SM on fewer registers.
+template <int D, int NT, int IT, int FMT>
 __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, int hs, int np, int lane) {
-    constexpr int KB = IT == 1 ? 32 : (IT >= 16 ? 1 : 16 / IT);
+    constexpr int KB = FMT ? (IT == 1 ? 8 : (IT >= 8 ? 1 : 8 / IT)) : (IT == 1 ? 32 : (IT >= 16 ? 1 : 16 / IT));
     const int base = p.uslot[u];
     const int nf = hs * D / 4;
     float m[IT], den[IT];
@@ -284,7 +285,7 @@ __device__ __forceinline__ void merge_task(const PlanParams& p, int u, int h0, i
 
 // The merge tasks dealt to warp w (w, w + Wtot, ...): each waits, bounded,
 // until its unit's pieces are all counted, merges its heads and publishes them.
-template <int D, int NT>
+template <int D, int NT, int FMT>
 __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int Wtot, int lane) {
     for (int k = w; k < p.ntasks; k += Wtot) {
         const int u = p.tunits[k / p.S];
@@ -308,11 +309,11 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (ok) {
             const int ni = (hs * D / 4 + 31) / 32;  // float4 items per lane
-            if (ni <= 1) merge_task<D, NT, 1>(p, u, h0, hs, np, lane);
-            else if (ni <= 2) merge_task<D, NT, 2>(p, u, h0, hs, np, lane);
-            else if (ni <= 4) merge_task<D, NT, 4>(p, u, h0, hs, np, lane);
-            else if (ni <= 8) merge_task<D, NT, 8>(p, u, h0, hs, np, lane);
-            else merge_task<D, NT, 16>(p, u, h0, hs, np, lane);
+            if (ni <= 1) merge_task<D, NT, 1, FMT>(p, u, h0, hs, np, lane);
+            else if (ni <= 2) merge_task<D, NT, 2, FMT>(p, u, h0, hs, np, lane);
+            else if (ni <= 4) merge_task<D, NT, 4, FMT>(p, u, h0, hs, np, lane);
+            else if (ni <= 8) merge_task<D, NT, 8, FMT>(p, u, h0, hs, np, lane);
+            else merge_task<D, NT, 16, FMT>(p, u, h0, hs, np, lane);
         }
         __syncwarp();
         if (lane == 0 && atomicAdd(&p.counters[p.U + u], 1u) == static_cast<unsigned int>(p.S - 1)) {
@@ -322,8 +323,11 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
     }
 }
 
+// FP8 pools: 6 CTAs (12 worker warps) per SM, measured 9% faster than 4 CTAs
+// on fewer registers (the FP8 page update is bound by per-warp latency, not by
+// bytes in flight).
 template <int D, int NT, int FMT>
-__global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(kPlanWarps * 32, FMT ? 6 : 1) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                          const PlanParams p) {
     constexpr int P = kPageTokens;
     constexpr int SB = plan_stage_bytes<D, FMT>();
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             zero_unit<D>(p, p.zunits[i], lane);
             publish_unit<D>(p, p.zunits[i], lane);
         }
-        run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
+        run_merge_tasks<D, NT, FMT>(p, w, gridDim.x * kPlanWarps, lane);
         gather_epilogue(p, lane);
         return;
     }
@@ -605,7 +609,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
                         // head groups of at most 8 float4 items per lane
                         constexpr int HG = 1024 / D;
                         for (int hg = 0; hg < p.G; hg += HG)
-                            merge_task<D, NT, (HG * D / 128 < NT * 8 * D / 128 ? HG * D / 128 : NT * 8 * D / 128)>(
+                            merge_task<D, NT, (HG * D / 128 < NT * 8 * D / 128 ? HG * D / 128 : NT * 8 * D / 128), FMT>(
                                 p, u, hg, min(HG, p.G - hg), npieces, lane);
                         if (lane == 0) p.counters[u] = 0u;
                     }
@@ -620,7 +624,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32) planned_decode_kernel(const _
             cu.next(p.uoff);
         }
     }
-    run_merge_tasks<D, NT>(p, w, gridDim.x * kPlanWarps, lane);
+    run_merge_tasks<D, NT, FMT>(p, w, gridDim.x * kPlanWarps, lane);
     gather_epilogue(p, lane);
 }
 

@@ -195,6 +195,7 @@ __device__ __forceinline__ void page_update_fp8(uint32_t sb, int valid, const ui
         const float p0 = ex2(x0 - nA), p1 = ex2(x1 - nB), p2 = ex2(x2 - nA), p3 = ex2(x3 - nB);
         st.l[nt][0] = st.l[nt][0] * aA + p0 + p2;
         st.l[nt][1] = st.l[nt][1] * aB + p1 + p3;
+        // unconditional: a warp vote to skip it when no max moved measured 3% slower
         const float cA = aA * ratio, cB = aB * ratio;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
