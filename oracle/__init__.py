@@ -251,6 +251,11 @@ def fp8_block_bytes(D, P=16):
     return 2 * P * D + 8 * P
 
 
+def _check_fp8_pool(pool_u8, g: Geom):
+    if pool_u8.dtype != np.uint8 or pool_u8.size != g.L * g.num_pages * g.Hkv * fp8_block_bytes(g.D, g.P):
+        raise ValueError("FP8 pool image does not match the geometry")
+
+
 def e4m3_encode(x):
     """Nearest-even E4M3 codes of fp32 values, finite overflow saturated to +-448."""
     x = np.ascontiguousarray(x, np.float32)
@@ -278,6 +283,7 @@ def fp8_quant_row(x):
 def append_fp8(pool_u8, g: Geom, layer, k, v, block_tables, positions):
     """In-place append of fp32 (or fp16, widened exactly) rows [B, T, Hkv, D] into
     a host byte image of an FP8 pool; returns 0 or -1 (bad entry skipped)."""
+    _check_fp8_pool(pool_u8, g)
     k = np.ascontiguousarray(np.asarray(k).astype(np.float32))
     v = np.ascontiguousarray(np.asarray(v).astype(np.float32))
     B, T = k.shape[0], k.shape[1]
@@ -290,6 +296,7 @@ def append_fp8(pool_u8, g: Geom, layer, k, v, block_tables, positions):
 
 def dequant_fp8(pool_u8, g: Geom):
     """fp32 [L, num_pages, Hkv, 2, P, D]: code * scale of every slot."""
+    _check_fp8_pool(pool_u8, g)
     out = np.empty((g.L, g.num_pages, g.Hkv, 2, g.P, g.D), np.float32)
     lib().or_dequant_fp8(np.ascontiguousarray(pool_u8).reshape(-1), g.L, g.Hkv, g.D, g.P, g.num_pages,
                          out.reshape(-1))
