@@ -326,3 +326,30 @@ def decode_fp8(pool_u8, g: Geom, layer, q, block_tables, seq_lens, scale=0.0):
             p = np.exp(s - s.max())
             out[b, h] = (p / p.sum()) @ V[h // G]
     return out
+
+
+def prefill_fp8(pool_u8, g: Geom, layer, q, block_tables, positions, scale=0.0):
+    """Chunked prefill over the dequantised FP8 cache: query token t of sequence
+    b at position positions[b] + t attends keys 0..positions[b] + t, the causal
+    row rule of cpu_attention (tests/test_attention.cu:66-97) in float64.
+    q: [B, T, Hq, D].  Returns float64 [B, T, Hq, D]."""
+    deq = dequant_fp8(pool_u8, g)[layer].astype(np.float64)  # [NP, Hkv, 2, P, D]
+    q = np.asarray(q).astype(np.float64)
+    B, T, Hq, D = q.shape
+    G = Hq // g.Hkv
+    sc = scale if scale > 0 else 1.0 / np.sqrt(D)
+    out = np.zeros((B, T, Hq, D))
+    for b in range(B):
+        n = int(positions[b]) + T
+        pages = np.asarray(block_tables[b][: (n + g.P - 1) // g.P])
+        kv = deq[pages]
+        K = kv[:, :, 0].transpose(1, 0, 2, 3).reshape(g.Hkv, -1, D)[:, :n]
+        V = kv[:, :, 1].transpose(1, 0, 2, 3).reshape(g.Hkv, -1, D)[:, :n]
+        rows = int(positions[b]) + np.arange(T)
+        hide = np.arange(n)[None, :] > rows[:, None]  # [T, n]
+        for h in range(Hq):
+            s = q[b, :, h] @ K[h // G].T * sc
+            s[hide] = -np.inf
+            p = np.exp(s - s.max(axis=1, keepdims=True))
+            out[b, :, h] = (p / p.sum(axis=1, keepdims=True)) @ V[h // G]
+    return out

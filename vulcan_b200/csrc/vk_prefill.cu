@@ -16,10 +16,18 @@
 //    S accumulator is re-used as the A operand of P V in registers; online
 //    softmax per row with quad shuffles; causal masking only on tiles that cross
 //    the diagonal; V of slots beyond the written tokens is zeroed in registers.
+//  * FP8 pools (FMT = 1, D = 128; block format in vk_fp8.cuh): a page block
+//    arrives in one bulk copy; K codes become the B operand of S through
+//    ldmatrix and a conversion, with Q's fragments loaded in the permuted
+//    contraction order of the decode (elements 4c..4c+3 per lane and 16-step);
+//    V codes become the B operand of P V without a transpose (element-major
+//    rows); K scales multiply the scores, V scales the probabilities (relative
+//    to a power of two per key tile, carried in the rescale of O).
 #include <cmath>
 #include <vector>
 
 #include "vk_internal.h"
+#include "vk_fp8.cuh"
 #include "vk_ptx.cuh"
 #include "vk_rope.cuh"
 
@@ -40,23 +48,27 @@ struct PrefillParams {
     int bt_stride, T, Hq, Hkv, G, L, layer, num_pages, q_tiles;
     float scale_log2;
     const float* rope_freq;  // non-null: q rotated (RoPE) at its position
+    // FP8 pools: block addressing for the bulk copies
+    const char* pool_base;
+    uint64_t seg_bytes, layer_off, head_bytes;
 };
 
-template <int D>
+template <int D, int FMT>
 __host__ __device__ constexpr int prefill_page_bytes() {
-    return 2 * kPageTokens * D * 2;
+    return FMT ? fp8_head_bytes(D) : 2 * kPageTokens * D * 2;
 }
 
-template <int D>
+template <int D, int FMT>
 __host__ __device__ constexpr int prefill_smem_bytes() {
-    return kPreStages * 4 * prefill_page_bytes<D>() + 2 * kPreStages * 8 + 1024;
+    return kPreStages * 4 * prefill_page_bytes<D, FMT>() + 2 * kPreStages * 8 + 1024;
 }
 
-template <int D>
+template <int D, int FMT>
 __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_constant__ CUtensorMap tmap,
                                                               const PrefillParams p) {
+    static_assert(FMT == 0 || D == kFp8Dim, "FP8 blocks are defined for head_dim 128");
     constexpr int P = kPageTokens;
-    constexpr int PB = prefill_page_bytes<D>();  // one page (K + V rows) in shared memory
+    constexpr int PB = prefill_page_bytes<D, FMT>();  // one page (K + V rows) in shared memory
     constexpr int SB = 4 * PB;                   // one 64-key stage
     constexpr int NB = D / 64;
     constexpr int KS = D / 16;                   // k-steps over the head dimension
@@ -92,7 +104,7 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
     if (warp == kPreWarps) {
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
-            prefetch_tmap(&tmap);
+            if (FMT == 0) prefetch_tmap(&tmap);
             const uint64_t pol = l2_evict_first_policy();
             const int32_t* btrow = p.bt + static_cast<int64_t>(b) * p.bt_stride;
             for (int j = 0; j < ntiles; ++j) {
@@ -107,10 +119,17 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
                         atomicOr(p.err, VK_ERR_PAGE_ID);
                         page = 0;
                     }
-                    const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
                     const uint32_t dst = smem_u32(smem + st * SB + i * PB);
+                    if constexpr (FMT == 1) {
+                        bulk_load(dst, p.pool_base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
+                                           static_cast<uint64_t>(hkv) * p.head_bytes,
+                                  PB, bar, pol);
+                    } else {
+                        const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
 #pragma unroll
-                    for (int hb = 0; hb < NB; ++hb) tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+                        for (int hb = 0; hb < NB; ++hb)
+                            tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+                    }
                 }
             }
         }
@@ -128,22 +147,26 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
             const __half* qlo = p.q + ((static_cast<int64_t>(b) * p.T + min(r_lo, p.T - 1)) * p.Hq + h) * D;
             const __half* qhi = p.q + ((static_cast<int64_t>(b) * p.T + min(r_hi, p.T - 1)) * p.Hq + h) * D;
             const bool vlo = r_lo < p.T, vhi = r_hi < p.T;
+            // the second pair of a lane's k-slots: elements d+8 (fp16 pages) or
+            // d+2 (FP8: the lane holds elements 4c..4c+3 of each 16-step)
+            constexpr int D2 = FMT ? 2 : 8;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                const int d = ks * 16 + 2 * c;
+                const int d = ks * 16 + (FMT ? 4 : 2) * c;
                 qa[ks][0] = vlo ? __ldg(reinterpret_cast<const unsigned int*>(qlo + d)) : 0u;
                 qa[ks][1] = vhi ? __ldg(reinterpret_cast<const unsigned int*>(qhi + d)) : 0u;
-                qa[ks][2] = vlo ? __ldg(reinterpret_cast<const unsigned int*>(qlo + d + 8)) : 0u;
-                qa[ks][3] = vhi ? __ldg(reinterpret_cast<const unsigned int*>(qhi + d + 8)) : 0u;
+                qa[ks][2] = vlo ? __ldg(reinterpret_cast<const unsigned int*>(qlo + d + D2)) : 0u;
+                qa[ks][3] = vhi ? __ldg(reinterpret_cast<const unsigned int*>(qhi + d + D2)) : 0u;
                 if (p.rope_freq != nullptr) {
                     qa[ks][0] = rope_word(qa[ks][0], d, qpos_lo, p.rope_freq);
                     qa[ks][1] = rope_word(qa[ks][1], d, qpos_hi, p.rope_freq);
-                    qa[ks][2] = rope_word(qa[ks][2], d + 8, qpos_lo, p.rope_freq);
-                    qa[ks][3] = rope_word(qa[ks][3], d + 8, qpos_hi, p.rope_freq);
+                    qa[ks][2] = rope_word(qa[ks][2], d + D2, qpos_lo, p.rope_freq);
+                    qa[ks][3] = rope_word(qa[ks][3], d + D2, qpos_hi, p.rope_freq);
                 }
             }
         }
         float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+        float vf = 1.f;  // FP8: acc holds the true sums divided by vf (a power of two)
         float acc[DT][4];
 #pragma unroll
         for (int n = 0; n < DT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
@@ -158,17 +181,66 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
             float s[8][4];
 #pragma unroll
             for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
+            if constexpr (FMT == 1) {
 #pragma unroll
                 for (int np = 0; np < 4; ++np) {  // keys [16*np, 16*np+16): page np
-                    const int kr = rr + (mi >> 1) * 8;
-                    const int d = ks * 16 + (mi & 1) * 8;
-                    uint32_t bk[4];
-                    ldsm_x4(bk, sb + np * PB + (d >> 6) * (2 * P * 128) + swz128(kr, (d & 63) >> 3));
-                    mma16816(s[2 * np], qa[ks], bk[0], bk[1]);
-                    mma16816(s[2 * np + 1], qa[ks], bk[2], bk[3]);
+#pragma unroll
+                    for (int kp = 0; kp < KS / 2; ++kp) {
+                        // matrices: keys 0-7 / 8-15 of 16-byte chunk 2kp, then of 2kp+1
+                        const int kr = rr + (mi & 1) * 8;
+                        const int ch = 2 * kp + (mi >> 1);
+                        uint32_t r[4], b0, b1;
+                        ldsm_x4(r, sb + np * PB + kr * D + ((ch ^ (kr & 7)) << 4));
+                        e4m3x4_to_h2x2(r[0], b0, b1);
+                        mma16816(s[2 * np], qa[2 * kp], b0, b1);
+                        e4m3x4_to_h2x2(r[1], b0, b1);
+                        mma16816(s[2 * np + 1], qa[2 * kp], b0, b1);
+                        e4m3x4_to_h2x2(r[2], b0, b1);
+                        mma16816(s[2 * np], qa[2 * kp + 1], b0, b1);
+                        e4m3x4_to_h2x2(r[3], b0, b1);
+                        mma16816(s[2 * np + 1], qa[2 * kp + 1], b0, b1);
+                    }
                 }
+            } else {
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+                    for (int np = 0; np < 4; ++np) {  // keys [16*np, 16*np+16): page np
+                        const int kr = rr + (mi >> 1) * 8;
+                        const int d = ks * 16 + (mi & 1) * 8;
+                        uint32_t bk[4];
+                        ldsm_x4(bk, sb + np * PB + (d >> 6) * (2 * P * 128) + swz128(kr, (d & 63) >> 3));
+                        mma16816(s[2 * np], qa[ks], bk[0], bk[1]);
+                        mma16816(s[2 * np + 1], qa[ks], bk[2], bk[3]);
+                    }
+                }
+            }
+
+            // FP8: per-key scales of the lane's keys (8-key group n, column
+            // 2c + e); keys at or beyond kv_len are unwritten (any bits)
+            float ksc[8][2], vsc[8][2];
+            float ratio = 1.f;
+            if constexpr (FMT == 1) {
+                float vmax = 0.f;
+#pragma unroll
+                for (int n = 0; n < 8; ++n)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int t = (n & 1) * 8 + 2 * c + e;  // token in page n/2
+                        const uint32_t blk = sb + (n >> 1) * PB;
+                        const bool ok = key0 + n * 8 + 2 * c + e < kv_len;
+                        ksc[n][e] = p.scale_log2 * lds_f32(blk + fp8_scale_off(0, t, D));
+                        vsc[n][e] = ok ? lds_f32(blk + fp8_scale_off(1, t, D)) : 0.f;
+                        vmax = fmaxf(vmax, vsc[n][e]);
+                    }
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+                const int ex = min(60, max(-60, static_cast<int>((__float_as_uint(vmax) >> 23) & 0xffu) - 127));
+                const float inv_f = __uint_as_float(static_cast<uint32_t>(127 - ex) << 23);  // 2^-ex
+                ratio = vf * inv_f;                                                           // exact
+                vf = __uint_as_float(static_cast<uint32_t>(127 + ex) << 23);
+#pragma unroll
+                for (int n = 0; n < 8; ++n) vsc[n][0] *= inv_f, vsc[n][1] *= inv_f;
             }
 
             // causal mask on tiles crossing this warp's diagonal
@@ -181,7 +253,7 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
                 for (int e = 0; e < 4; ++e) {
                     const int key = k0 + (e & 1);
                     const int qp = e < 2 ? qpos_lo : qpos_hi;
-                    float v = s[n][e] * p.scale_log2;
+                    float v = s[n][e] * (FMT ? ksc[n][e & 1] : p.scale_log2);
                     if (need_mask && key > qp) v = -INFINITY;
                     s[n][e] = v;
                 }
@@ -205,21 +277,50 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
                 const float p2 = ex2(s[n][2] - n_hi), p3 = ex2(s[n][3] - n_hi);
                 ps_lo += p0 + p1;
                 ps_hi += p2 + p3;
-                pa[n >> 1][(n & 1) * 2 + 0] = pack_half2(p0, p1);
-                pa[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2, p3);
+                if constexpr (FMT == 1) {  // times each key's V scale (relative to vf)
+                    pa[n >> 1][(n & 1) * 2 + 0] = pack_half2(p0 * vsc[n][0], p1 * vsc[n][1]);
+                    pa[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2 * vsc[n][0], p3 * vsc[n][1]);
+                } else {
+                    pa[n >> 1][(n & 1) * 2 + 0] = pack_half2(p0, p1);
+                    pa[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2, p3);
+                }
             }
             l_lo = l_lo * a_lo + ps_lo;
             l_hi = l_hi * a_hi + ps_hi;
+            const float c_lo = FMT ? a_lo * ratio : a_lo, c_hi = FMT ? a_hi * ratio : a_hi;
 #pragma unroll
             for (int n = 0; n < DT; ++n) {
-                acc[n][0] *= a_lo;
-                acc[n][1] *= a_lo;
-                acc[n][2] *= a_hi;
-                acc[n][3] *= a_hi;
+                acc[n][0] *= c_lo;
+                acc[n][1] *= c_lo;
+                acc[n][2] *= c_hi;
+                acc[n][3] *= c_hi;
             }
 
             // O[16 x D] += P[16 x 64] V[64 x D]
             const bool tail = key0 + kPreKeys > kv_len;
+            if constexpr (FMT == 1) {
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    uint32_t keep0 = 0xffffffffu, keep1 = 0xffffffffu;  // keys 2c, 2c+1 / 2c+8, 2c+9
+                    if (tail) {
+                        const int t0 = key0 + kk * 16 + 2 * c;
+                        keep0 = (t0 < kv_len ? 0x0000ffffu : 0u) | (t0 + 1 < kv_len ? 0xffff0000u : 0u);
+                        keep1 = (t0 + 8 < kv_len ? 0x0000ffffu : 0u) | (t0 + 9 < kv_len ? 0xffff0000u : 0u);
+                    }
+#pragma unroll
+                    for (int dq = 0; dq < D / 32; ++dq) {
+                        // matrices: element rows 32dq + 8i + 0..7 (16 bytes each), output tiles 4dq + i
+                        uint32_t r[4];
+                        ldsm_x4(r, sb + kk * PB + P * D + (32 * dq + 8 * mi + rr) * P);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            uint32_t b0, b1;
+                            e4m3x4_to_h2x2(r[i], b0, b1);
+                            mma16816(acc[4 * dq + i], pa[kk], b0 & keep0, b1 & keep1);
+                        }
+                    }
+                }
+            } else {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -241,6 +342,7 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
                     mma16816(acc[2 * dp + 1], pa[kk], bv[2], bv[3]);
                 }
             }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
         }
@@ -250,7 +352,7 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
             l_lo += __shfl_xor_sync(0xffffffffu, l_lo, o);
             l_hi += __shfl_xor_sync(0xffffffffu, l_hi, o);
         }
-        const float i_lo = 1.f / l_lo, i_hi = 1.f / l_hi;
+        const float i_lo = (FMT ? vf : 1.f) / l_lo, i_hi = (FMT ? vf : 1.f) / l_hi;
         __half* olo = p.out + ((static_cast<int64_t>(b) * p.T + r_lo) * p.Hq + h) * D;
         __half* ohi = p.out + ((static_cast<int64_t>(b) * p.T + r_hi) * p.Hq + h) * D;
 #pragma unroll
@@ -262,18 +364,18 @@ __global__ void __launch_bounds__(kPreThreads) prefill_kernel(const __grid_const
     }
 }
 
-template <int D>
+template <int D, int FMT>
 static vk_status launch_prefill_t(vk_pool* pool, const PrefillParams& p, int B, cudaStream_t st) {
-    constexpr int smem = prefill_smem_bytes<D>();
+    constexpr int smem = prefill_smem_bytes<D, FMT>();
     static uint64_t attr_set = 0;
     const uint64_t bit = 1ull << (pool->device & 63);
     if (!(attr_set & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill)");
         attr_set |= bit;
     }
     dim3 grid(p.q_tiles, p.Hq, B);
-    prefill_kernel<D><<<grid, kPreThreads, smem, st>>>(pool->tmap, p);
+    prefill_kernel<D, FMT><<<grid, kPreThreads, smem, st>>>(pool->tmap, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "prefill_kernel launch");
 }
@@ -287,8 +389,8 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
                                 const int32_t* positions, int32_t batch, int32_t tokens,
                                 int32_t num_q_heads, float scale, void* stream) {
     if (!pool) return fail(VK_INVALID_ARG, "pool is NULL");
-    if (pool->kv && pool->kv_format != VK_KV_FP16) return fail(VK_UNSUPPORTED, "prefill reads fp16 pages only");
-    if (!pool->kv || !pool->tmap_ok) return fail(VK_UNSUPPORTED, "prefill needs a KV pool addressable by TMA");
+    const bool fp8 = pool->kv && pool->kv_format == VK_KV_FP8;
+    if (!pool->kv || (!fp8 && !pool->tmap_ok)) return fail(VK_UNSUPPORTED, "prefill needs a KV pool addressable by TMA");
     if (pool->cfg.page_tokens != kPageTokens) return fail(VK_UNSUPPORTED, "prefill supports page_tokens == 16");
     const int D = pool->cfg.head_dim, Hkv = pool->cfg.num_kv_heads;
     if (D != 64 && D != 128) return fail(VK_UNSUPPORTED, "prefill supports head_dim 64 and 128");
@@ -316,16 +418,24 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
     p.num_pages = pool->num_pages;
     p.q_tiles = (tokens + kPreRows - 1) / kPreRows;
     p.rope_freq = pool->rope_freq;
+    p.pool_base = pool->base;
+    p.seg_bytes = pool->seg_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
+    p.head_bytes = pool->head_bytes;
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
+    if (fp8) {  // FP8 pages (head_dim 128): the mma.sync kernel; the tcgen05 one reads fp16 tiles
+        if (pool->prefill_path == 2) return fail(VK_UNSUPPORTED, "the tcgen05 prefill reads fp16 pages only");
+        return launch_prefill_t<128, 1>(pool, p, batch, st);
+    }
     const bool tc = D == 128 && pool->prefill_path != 1;
     if (pool->prefill_path == 2 && !tc) return fail(VK_UNSUPPORTED, "the tcgen05 prefill supports head_dim 128");
     if (tc)
         return prefill_tc(pool, layer, q, out, block_tables, bt_stride, positions, batch, tokens, num_q_heads, scale,
                           st);
-    return D == 128 ? launch_prefill_t<128>(pool, p, batch, st) : launch_prefill_t<64>(pool, p, batch, st);
+    return D == 128 ? launch_prefill_t<128, 0>(pool, p, batch, st) : launch_prefill_t<64, 0>(pool, p, batch, st);
 }
 
 extern "C" vk_status vk_set_rope(vk_pool* pool, float theta_base) {
