@@ -109,6 +109,20 @@ def algorithmic_bytes(ctx, Hq, Hkv, D, kv_format="fp16"):
     return dict(decode=kv + qo + table, append=new, total=kv + new + qo + table)
 
 
+def fill_fp8(pool, D, dev, gen):
+    """Fills an FP8 pool with e4m3 codes of N(0, 0.5^2) rows at the scale of
+    their quantisation (max|x| ~ 1.4 over 128 values), every code finite."""
+    import torch
+    blocks = pool.block_view().view(-1, pool.block_bytes)
+    codes_b = 2 * PAGE * D
+    for s in range(0, blocks.shape[0], 1 << 16):
+        part = blocks[s:s + (1 << 16)]
+        x = torch.randn(part.shape[0], codes_b, device=dev, generator=gen) * (0.5 * 448.0 / 1.4)
+        part[:, :codes_b].copy_(x.clamp_(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8))
+        sc = torch.full((part.shape[0], 2 * PAGE), 1.4 / 448.0, device=dev, dtype=torch.float32)
+        part[:, codes_b:].copy_(sc.view(torch.uint8))
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -340,16 +354,7 @@ def main():
             part = flat[s:s + chunk]
             part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
     else:
-        # e4m3 codes of N(0, 0.5^2) rows at the scale of their quantisation
-        # (max|x| ~ 1.4 over 128 values), every code finite
-        blocks = pool.block_view().view(-1, pool.block_bytes)
-        codes_b = 2 * PAGE * D
-        for s in range(0, blocks.shape[0], 1 << 16):
-            part = blocks[s:s + (1 << 16)]
-            x = torch.randn(part.shape[0], codes_b, device=dev, generator=gen) * (0.5 * 448.0 / 1.4)
-            part[:, :codes_b].copy_(x.clamp_(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8))
-            sc = torch.full((part.shape[0], 2 * PAGE), 1.4 / 448.0, device=dev, dtype=torch.float32)
-            part[:, codes_b:].copy_(sc.view(torch.uint8))
+        fill_fp8(pool, D, dev, gen)
     bt_d = torch.from_numpy(bt).to(dev)
     pos_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     lens_d = torch.from_numpy(lens).to(dev)
@@ -730,13 +735,16 @@ def run_prefill(args, wl):
     ctx = wl["ctx"][seqs]
     Bl = len(seqs)
     bt, num_pages = layout(ctx + T - 1, wl["seed"] + rank, slack=1.0)
-    pool = vk.PagedKVPool(L, H, D, num_pages, zero=False)
+    pool = vk.PagedKVPool(L, H, D, num_pages, zero=False, kv_format=args.kv)
     gen = torch.Generator(device=dev)
     gen.manual_seed(5 + rank)
-    flat = pool.storage.view(torch.float16)
-    for s0 in range(0, flat.numel(), 1 << 28):
-        part = flat[s0:s0 + (1 << 28)]
-        part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    if args.kv == "fp16":
+        flat = pool.storage.view(torch.float16)
+        for s0 in range(0, flat.numel(), 1 << 28):
+            part = flat[s0:s0 + (1 << 28)]
+            part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    else:
+        fill_fp8(pool, D, dev, gen)
     bt_d = torch.from_numpy(bt).to(dev)
     pos_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
     q = (torch.randn(Bl, T, H, D, device=dev, generator=gen) * 0.5).half()
@@ -790,9 +798,11 @@ def run_prefill(args, wl):
     flops_job = prefill_flops(wl["ctx"], T, H, D)
     # ncu traffic of the 2-sequence capture scaled by the K/V tiles this launch reads
     full_wl = workload("prefill")
-    traffic = NCU_PREFILL_2SEQ_BYTES * prefill_tile_reads(ctx, T) / prefill_tile_reads(full_wl["ctx"][:2], T)
-    traffic_src = ("ncu capture of the first 2 sequences (1 layer), scaled by K/V tiles read: "
-                   "profiles/prefill_tc_kernel_small-case_full.md")
+    traffic, traffic_src = None, None
+    if args.kv == "fp16":
+        traffic = NCU_PREFILL_2SEQ_BYTES * prefill_tile_reads(ctx, T) / prefill_tile_reads(full_wl["ctx"][:2], T)
+        traffic_src = ("ncu capture of the first 2 sequences (1 layer), scaled by K/V tiles read: "
+                       "profiles/prefill_tc_kernel_small-case_full.md")
     peak_t = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     achieved = flops_local / (launch_ms * 1e-3) / 1e12
@@ -800,8 +810,13 @@ def run_prefill(args, wl):
         line = {"metric": "chunked prefill (append + causal attention) tokens/s and TFLOP/s",
                 "value": B * T / (ms_step * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,0.5^2) fp16)",
-                "config": {"workload": wl["desc"], "launch": "CUDA graph of the %d-layer step" % L,
+                "vs_baseline": None,
+                "dtype": "f16" if args.kv == "fp16" else "e4m3 K/V pages (fp32 scale per row), f16 MMA, f32 accumulation",
+                "data": "synthetic (seeded N(0,0.5^2) fp16)",
+                "config": {"workload": wl["desc"], "kv_format": args.kv,
+                           "kernel": ("mma.sync FP8-page kernel" if args.kv == "fp8" else
+                                      "tcgen05 kernel" if wl["D"] == 128 else "mma.sync kernel"),
+                           "launch": "CUDA graph of the %d-layer step" % L,
                            "shard": "sequence x%d" % world if world > 1 else "none"},
                 "attn_tflops": flops_job * L / (ms_step * 1e-3) / 1e12,
                 "gpu_launches": 2 * L * args.steps, "clocks": clk.summary(),
