@@ -96,9 +96,9 @@ vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t byt
  * tokens of a row in the order 0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15, then 16
  * K and 16 V scales.  head_dim 128 and page_tokens 16 only.  FP8 pools take
  * vk_append, vk_append_f32 (quantising), the planned decode (vk_decode_plan_*,
- * vk_decode_run, fused append included), vk_prefill (its mma.sync kernel;
- * prefill path 2 is refused), allocation, copy and swap; vk_decode and
- * vk_decode_static return VK_UNSUPPORTED. */
+ * vk_decode_run, fused append included), vk_decode and vk_decode_static,
+ * vk_prefill (its mma.sync kernel; prefill path 2 is refused), allocation,
+ * copy and swap. */
 #define VK_KV_FP16 0
 #define VK_KV_FP8  1
 

@@ -4,7 +4,8 @@ oracle's restatement (oracle/vk_oracle.c: or_append_fp8, or_dequant_fp8).
 Append, fused append and page copy are bit-exact against the oracle on the
 whole byte image of the pool (unwritten slots hold random bytes on both
 sides).  Decode outputs are compared with the oracle's float64 attention over
-the dequantised cache under the fp16 attention tolerance."""
+the dequantised cache under the fp16 attention tolerance; prefill outputs
+likewise (oracle.prefill_fp8)."""
 import numpy as np
 import pytest
 import torch
@@ -158,6 +159,28 @@ def test_fp8_decode_rope(vk):
         assert (np.abs(a[:, 0] - h[:, 0]) <= 1.01 * step + 1e-6).all(), "K rows with RoPE"
 
 
+@pytest.mark.parametrize("pps", [0, 2])
+def test_fp8_split_decode(vk, pps):
+    """The split-grid decode (callers without host lengths) on FP8 pages, one
+    split per sequence or two pages per split with the merge kernel."""
+    rng = np.random.default_rng(93 + pps)
+    Hkv, D, L, layer, G = 2, 128, 2, 0, 8
+    Hq = G * Hkv
+    lens = np.array([1, 16, 33, 700], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool, host = fp8_pool(vk, g, rng)
+    fill_history(vk, pool, host, g, rng, layer, bt, lens + 1)  # tokens 0 .. len-1
+    pool.set_split(pps)
+    q = rows(rng, len(lens), Hq, D)
+    out = pool.decode(layer, dev_f16(q), dev_i32(bt), dev_i32(lens), int(lens.max()))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert_bytes(pool, host, "FP8 history append")
+    ref = oracle.decode_fp8(host, g, layer, q, bt, lens)
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 split decode, pages per split %d" % pps)
+
+
 @pytest.mark.parametrize("rope", [False, True])
 def test_fp8_prefill(vk, rope):
     """Chunked prefill over FP8 pages (the mma.sync kernel): the chunk's rows are
@@ -222,10 +245,6 @@ def test_fp8_unsupported_entry_points(vk):
     rng = np.random.default_rng(87)
     g = oracle.Geom(1, 1, 128, 16, 4)
     pool, _ = fp8_pool(vk, g, rng)
-    q = dev_f16(rows(rng, 1, 8, 128))
-    bt = dev_i32([[0, 1]])
-    with pytest.raises(vk.VKError):
-        pool.decode(0, q, bt, dev_i32([20]), 20)
     with pytest.raises(RuntimeError):
         pool.kv_view()
     with pytest.raises(vk.VKError):

@@ -26,8 +26,11 @@
 //    normalised partial and log-sum-exp and the merge kernel combines them.
 //  * Every wait is bounded; bad block-table entries are recorded in the pool's
 //    error word and replaced by page 0 so no access leaves the pool.
+//  * FP8 pools (FMT = 1, D = 128): a page block arrives in one bulk copy and
+//    the consumers fold it in with page_update_fp8 (vk_fp8.cuh).
 #include <algorithm>
 
+#include "vk_fp8.cuh"
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
 #include "vk_rope.cuh"
@@ -49,16 +52,19 @@ struct DecodeParams {
     int bt_stride, Hq, Hkv, G, L, layer, num_pages, pps, max_splits;
     float scale_log2;
     const float* rope_freq;  // non-null: q rotated (RoPE) at position seq_len - 1
+    // FP8 pools: block addressing for the bulk copies
+    const char* pool_base;
+    uint64_t seg_bytes, layer_off, head_bytes;
 };
 
-template <int D>
+template <int D, int FMT>
 __host__ __device__ constexpr int stage_bytes() {
-    return 2 * kPageTokens * D * 2;
+    return FMT ? fp8_head_bytes(D) : 2 * kPageTokens * D * 2;
 }
 
-template <int D>
+template <int D, int FMT>
 __host__ __device__ constexpr int decode_smem_bytes() {
-    return kDecodeStages * stage_bytes<D>() + 2 * kDecodeStages * 8 + 1024;
+    return kDecodeStages * stage_bytes<D, FMT>() + 2 * kDecodeStages * 8 + 1024;
 }
 
 // Length of sequence b clamped to the table capacity, recording bad lengths.
@@ -71,11 +77,14 @@ __device__ __forceinline__ int checked_len(const DecodeParams& p, int b, bool re
     return n;
 }
 
-template <int D, int NT>
+template <int D, int NT, int FMT>
 __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                 const DecodeParams p) {
+    static_assert(FMT == 0 || D == kFp8Dim, "FP8 blocks are defined for head_dim 128");
+    // the combine after the ring reuses its shared memory
+    static_assert(kDecodeStages * stage_bytes<D, FMT>() >= 4 * (2 + D) * NT * 8 * 4, "combine does not fit");
     constexpr int P = kPageTokens;
-    constexpr int SB = stage_bytes<D>();
+    constexpr int SB = stage_bytes<D, FMT>();
     constexpr int NB = D / 64;   // 128-byte TMA boxes per row
     constexpr int KS = D / 16;   // k-steps of S^T, m-tiles of O^T
     constexpr int NH = NT * 8;   // query heads per CTA tile (>= G)
@@ -124,7 +133,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
     if (warp == kDecodeConsumers) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            prefetch_tmap(&tmap);
+            if (FMT == 0) prefetch_tmap(&tmap);
             const uint64_t pol = l2_evict_first_policy();
             const int32_t* btrow = p.bt + static_cast<int64_t>(b) * p.bt_stride + pbeg;
             for (int i = 0; i < n; ++i) {
@@ -137,17 +146,27 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
                     atomicOr(p.err, VK_ERR_PAGE_ID);
                     page = 0;
                 }
-                const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
                 const uint32_t bar = smem_u32(&full[st]);
                 mbar_expect_tx(bar, SB);
                 const uint32_t dst = smem_u32(smem + st * SB);
+                if constexpr (FMT == 1) {
+                    bulk_load(dst, p.pool_base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
+                                       static_cast<uint64_t>(hkv) * p.head_bytes,
+                              SB, bar, pol);
+                } else {
+                    const int row = ((p.layer * p.num_pages + page) * p.Hkv + hkv) * (2 * P);
 #pragma unroll
-                for (int hb = 0; hb < NB; ++hb) tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+                    for (int hb = 0; hb < NB; ++hb)
+                        tma_load_2d(dst + hb * (2 * P * 128), &tmap, hb * 64, row, bar, pol);
+                }
             }
         }
     } else {
         // ------------------------------------------------------------ consumers
         // Q as the B operand (k = head dim, n = query head): 2 regs per k-step.
+        // (FP8: the permuted contraction order of page_update_fp8, elements
+        // 4c..4c+3 of each 16-step, so the second pair is at d+2)
+        constexpr int D2 = FMT ? 2 : 8;
         uint32_t qf[NT][KS][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -156,9 +175,9 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
             const __half* qrow = p.q + (static_cast<int64_t>(b) * p.Hq + hkv * p.G + (ok ? hl : 0)) * D;
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
-                const int d = ks * 16 + (lane & 3) * 2;
+                const int d = ks * 16 + (lane & 3) * (FMT ? 4 : 2);
                 qf[nt][ks][0] = ok ? *reinterpret_cast<const uint32_t*>(qrow + d) : 0u;
-                qf[nt][ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + d + 8) : 0u;
+                qf[nt][ks][1] = ok ? *reinterpret_cast<const uint32_t*>(qrow + d + D2) : 0u;
             }
         }
         if (p.rope_freq != nullptr) {  // fused RoPE at the new token's position
@@ -166,11 +185,13 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int ks = 0; ks < KS; ++ks) {
-                    const int d = ks * 16 + (lane & 3) * 2;
+                    const int d = ks * 16 + (lane & 3) * (FMT ? 4 : 2);
                     qf[nt][ks][0] = rope_word(qf[nt][ks][0], d, seq_len - 1, p.rope_freq);
-                    qf[nt][ks][1] = rope_word(qf[nt][ks][1], d + 8, seq_len - 1, p.rope_freq);
+                    qf[nt][ks][1] = rope_word(qf[nt][ks][1], d + D2, seq_len - 1, p.rope_freq);
                 }
         }
+        WarpSoftmaxState<D, NT> st8;  // FP8 pages: page_update_fp8's state
+        if constexpr (FMT == 1) st8.reset();
         const int g8 = lane >> 2;           // token row of this lane in S^T (and +8)
         const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix index, row in matrix
         bool alive = true;
@@ -183,6 +204,12 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
             }
             const uint32_t sb = smem_u32(smem + st * SB);
             const int valid = min(P, seq_len - (pbeg + i) * P);
+            if constexpr (FMT == 1) {
+                page_update_fp8<D, NT>(sb, valid, qf, st8, p.scale_log2, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+                continue;
+            }
 
             // S^T[16 tokens x 8 heads] = K Q^T
             float s[NT][4];
@@ -252,6 +279,20 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_kernel(const __grid_con
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+        }
+        if constexpr (FMT == 1) {  // back to this kernel's state, acc in true units
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    m_run[nt][j] = st8.m[nt][j];
+                    l_run[nt][j] = st8.l[nt][j];
+                }
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[nt][mt][e] = st8.acc[nt][mt][e] * st8.vf;
+            }
         }
         // Row sums: reduce over the 8 lanes sharing lane&3.
 #pragma unroll
@@ -349,18 +390,18 @@ int decode_pages_per_split(const vk_pool* pool, int B, int max_seq_len) {
     return pps;
 }
 
-template <int D, int NT>
+template <int D, int NT, int FMT>
 static vk_status launch_decode_t(vk_pool* pool, const DecodeParams& p, int B, cudaStream_t st) {
-    constexpr int smem = decode_smem_bytes<D>();
+    constexpr int smem = decode_smem_bytes<D, FMT>();
     static uint64_t attr_set = 0;  // one bit per device ordinal
     const uint64_t bit = 1ull << (pool->device & 63);
     if (!(attr_set & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
         attr_set |= bit;
     }
     dim3 grid(p.max_splits, p.Hkv, B);
-    decode_kernel<D, NT><<<grid, kDecodeThreads, smem, st>>>(pool->tmap, p);
+    decode_kernel<D, NT, FMT><<<grid, kDecodeThreads, smem, st>>>(pool->tmap, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "decode_kernel launch");
     if (p.max_splits > 1) {
@@ -407,9 +448,8 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
                     void* workspace, size_t workspace_bytes, void* stream) {
     if (!pool) return fail(VK_INVALID_ARG, "pool is NULL");
     if (!pool->kv) return fail(VK_UNSUPPORTED, "decode needs a KV pool (page_bytes == 0)");
-    if (pool->kv_format != VK_KV_FP16)
-        return fail(VK_UNSUPPORTED, "vk_decode reads fp16 pages; FP8 pools decode through vk_decode_run");
-    if (!pool->tmap_ok) return fail(VK_UNSUPPORTED, "pool too large for 32-bit TMA row coordinates");
+    const bool fp8 = pool->kv_format == VK_KV_FP8;
+    if (!fp8 && !pool->tmap_ok) return fail(VK_UNSUPPORTED, "pool too large for 32-bit TMA row coordinates");
     if (pool->cfg.page_tokens != kPageTokens) return fail(VK_UNSUPPORTED, "decode supports page_tokens == 16");
     const int D = pool->cfg.head_dim, Hkv = pool->cfg.num_kv_heads;
     if (D != 64 && D != 128 && D != 256) return fail(VK_UNSUPPORTED, "decode supports head_dim 64, 128, 256");
@@ -444,6 +484,10 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(D));
     p.scale_log2 = sc * 1.4426950408889634f;
     p.rope_freq = pool->rope_freq;
+    p.pool_base = pool->base;
+    p.seg_bytes = pool->seg_bytes;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
+    p.head_bytes = pool->head_bytes;
     p.ws_o = nullptr;
     p.ws_lse = nullptr;
     if (p.max_splits > 1) {
@@ -455,9 +499,12 @@ vk_status vk_decode(vk_pool* pool, int32_t layer, const void* q, void* out,
     }
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
-    if (D == 128) return G <= 8 ? launch_decode_t<128, 1>(pool, p, batch, st) : launch_decode_t<128, 2>(pool, p, batch, st);
-    if (D == 64) return G <= 8 ? launch_decode_t<64, 1>(pool, p, batch, st) : launch_decode_t<64, 2>(pool, p, batch, st);
-    return G <= 8 ? launch_decode_t<256, 1>(pool, p, batch, st) : launch_decode_t<256, 2>(pool, p, batch, st);
+    if (fp8)  // FP8 pools have head_dim 128
+        return G <= 8 ? launch_decode_t<128, 1, 1>(pool, p, batch, st) : launch_decode_t<128, 2, 1>(pool, p, batch, st);
+    if (D == 128)
+        return G <= 8 ? launch_decode_t<128, 1, 0>(pool, p, batch, st) : launch_decode_t<128, 2, 0>(pool, p, batch, st);
+    if (D == 64) return G <= 8 ? launch_decode_t<64, 1, 0>(pool, p, batch, st) : launch_decode_t<64, 2, 0>(pool, p, batch, st);
+    return G <= 8 ? launch_decode_t<256, 1, 0>(pool, p, batch, st) : launch_decode_t<256, 2, 0>(pool, p, batch, st);
 }
 
 }  // extern "C"
