@@ -6,7 +6,7 @@
 // pos = positions[b]+t goes to page block_tables[b][pos/16], slot pos%16, for
 // every KV head.  The reference issues 2*Hkv*T blocking cudaMemcpy calls; here
 // one launch moves every row with 16-byte vector loads and stores, one warp per
-// (token, kv head) covering its K row and V row.
+// (token, group of 4 KV heads) covering their K rows and V rows.
 #include "vk_internal.h"
 #include "vk_fp8.cuh"
 #include "vk_ptx.cuh"
@@ -26,16 +26,21 @@ struct AppendParams {
     const float* rope_freq;  // non-null: K rows are rotated (RoPE) at their positions
 };
 
+constexpr int kAppendHeads = 4;  // KV heads per warp: their rows' loads are in flight together
+
+// One warp per (token, group of 4 KV heads): the position checks and the page
+// lookup once, then the K and V rows of the group's heads, every load of a
+// pass issued before its first store (2 KiB per warp in flight at D=128).
 template <bool F32>
 __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
-    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t rows = static_cast<int64_t>(p.B) * p.T * p.Hkv;
-    if (row >= rows) return;
-    const int h = static_cast<int>(row % p.Hkv);
-    const int64_t bt_idx = row / p.Hkv;  // b*T + t
-    const int t = static_cast<int>(bt_idx % p.T);
-    const int b = static_cast<int>(bt_idx / p.T);
+    const int groups = (p.Hkv + kAppendHeads - 1) / kAppendHeads;
+    if (wid >= static_cast<int64_t>(p.B) * p.T * groups) return;
+    const int h0 = static_cast<int>(wid % groups) * kAppendHeads;
+    const int64_t tok = wid / groups;  // b*T + t
+    const int t = static_cast<int>(tok % p.T);
+    const int b = static_cast<int>(tok / p.T);
     const int pos = p.pos[b] + t;
     if (pos < 0 || pos / p.P >= p.bt_stride) {
         if (lane == 0) atomicOr(p.err, VK_ERR_TABLE_INDEX);
@@ -46,40 +51,59 @@ __global__ void __launch_bounds__(256) append_kernel(const AppendParams p) {
         if (lane == 0) atomicOr(p.err, VK_ERR_PAGE_ID);
         return;
     }
-    char* dst_k = p.base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
-                  static_cast<uint64_t>(h) * p.head_bytes +
-                  static_cast<uint64_t>(pos % p.P) * p.D * 2;
-    char* dst_v = dst_k + static_cast<uint64_t>(p.P) * p.D * 2;
-    const int vec_per_row = p.D / 8;  // 8 fp16 = 16 bytes per vector
-    const int64_t src_elem = row * p.D;
-    for (int i = lane; i < 2 * vec_per_row; i += 32) {
-        const bool is_v = i >= vec_per_row;
-        const int vi = is_v ? i - vec_per_row : i;
-        uint4 val;
-        if constexpr (F32) {
-            const float4* src =
-                reinterpret_cast<const float4*>(static_cast<const float*>(is_v ? p.v : p.k) + src_elem) +
-                2 * vi;
-            float4 a = __ldg(src), c = __ldg(src + 1);
-            if (!is_v && p.rope_freq != nullptr) {  // rotate in fp32, then round
-                const int i0 = vi * 4;
-                float2 r;
-                r = rope_pair(a.x, a.y, i0, pos, p.rope_freq); a.x = r.x; a.y = r.y;
-                r = rope_pair(a.z, a.w, i0 + 1, pos, p.rope_freq); a.z = r.x; a.w = r.y;
-                r = rope_pair(c.x, c.y, i0 + 2, pos, p.rope_freq); c.x = r.x; c.y = r.y;
-                r = rope_pair(c.z, c.w, i0 + 3, pos, p.rope_freq); c.z = r.x; c.w = r.y;
+    char* dst0 = p.base + p.layer_off + static_cast<uint64_t>(page) * p.seg_bytes +
+                 static_cast<uint64_t>(pos % p.P) * p.D * 2;
+    const int vpr = p.D / 8;  // 16-byte vectors per row (8 fp16)
+    // vectors [i0, i0 + 64) of each head's K|V rows per pass (one pass for D <= 256)
+    for (int i0 = 0; i0 < 2 * vpr; i0 += 64) {
+    uint4 val[kAppendHeads][2];
+#pragma unroll
+    for (int j = 0; j < kAppendHeads; ++j) {
+        const int h = h0 + j;
+        const int64_t src_elem = (tok * p.Hkv + h) * p.D;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = i0 + lane + 32 * k;
+            if (h >= p.Hkv || i >= 2 * vpr) continue;
+            const bool is_v = i >= vpr;
+            const int vi = is_v ? i - vpr : i;
+            if constexpr (F32) {
+                const float4* src =
+                    reinterpret_cast<const float4*>(static_cast<const float*>(is_v ? p.v : p.k) + src_elem) + 2 * vi;
+                float4 a = __ldg(src), c = __ldg(src + 1);
+                if (!is_v && p.rope_freq != nullptr) {  // rotate in fp32, then round
+                    const int i0 = vi * 4;
+                    float2 r;
+                    r = rope_pair(a.x, a.y, i0, pos, p.rope_freq); a.x = r.x; a.y = r.y;
+                    r = rope_pair(a.z, a.w, i0 + 1, pos, p.rope_freq); a.z = r.x; a.w = r.y;
+                    r = rope_pair(c.x, c.y, i0 + 2, pos, p.rope_freq); c.x = r.x; c.y = r.y;
+                    r = rope_pair(c.z, c.w, i0 + 3, pos, p.rope_freq); c.z = r.x; c.w = r.y;
+                }
+                val[j][k].x = pack_half2(a.x, a.y);
+                val[j][k].y = pack_half2(a.z, a.w);
+                val[j][k].z = pack_half2(c.x, c.y);
+                val[j][k].w = pack_half2(c.z, c.w);
+            } else {
+                const uint4* src =
+                    reinterpret_cast<const uint4*>(static_cast<const __half*>(is_v ? p.v : p.k) + src_elem) + vi;
+                val[j][k] = __ldg(src);
+                if (!is_v && p.rope_freq != nullptr) val[j][k] = rope_uint4(val[j][k], vi * 8, pos, p.rope_freq);
             }
-            val.x = pack_half2(a.x, a.y);
-            val.y = pack_half2(a.z, a.w);
-            val.z = pack_half2(c.x, c.y);
-            val.w = pack_half2(c.z, c.w);
-        } else {
-            const uint4* src =
-                reinterpret_cast<const uint4*>(static_cast<const __half*>(is_v ? p.v : p.k) + src_elem) + vi;
-            val = __ldg(src);
-            if (!is_v && p.rope_freq != nullptr) val = rope_uint4(val, vi * 8, pos, p.rope_freq);
         }
-        reinterpret_cast<uint4*>(is_v ? dst_v : dst_k)[vi] = val;
+    }
+#pragma unroll
+    for (int j = 0; j < kAppendHeads; ++j) {
+        const int h = h0 + j;
+        char* dst_k = dst0 + static_cast<uint64_t>(h) * p.head_bytes;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = i0 + lane + 32 * k;
+            if (h >= p.Hkv || i >= 2 * vpr) continue;
+            const bool is_v = i >= vpr;
+            const int vi = is_v ? i - vpr : i;
+            reinterpret_cast<uint4*>(dst_k + (is_v ? static_cast<uint64_t>(p.P) * p.D * 2 : 0))[vi] = val[j][k];
+        }
+    }
     }
 }
 
@@ -108,7 +132,8 @@ vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, 
     p.P = pool->cfg.page_tokens;
     p.num_pages = pool->num_pages;
     p.rope_freq = pool->kv ? pool->rope_freq : nullptr;
-    const int64_t threads = static_cast<int64_t>(B) * T * p.Hkv * 32;
+    const int64_t groups = (p.Hkv + kAppendHeads - 1) / kAppendHeads;
+    const int64_t threads = static_cast<int64_t>(B) * T * groups * 32;
     const int64_t blocks = (threads + 255) / 256;
     if (blocks > 0x7fffffff) return fail(VK_INVALID_ARG, "append too large for one launch");
     if (f32)
