@@ -103,6 +103,9 @@ class PagedKVPool:
                                                               ctypes.byref(handle)), "vk_pool_create_in")
         if self.kv and self._lib.vk_pool_kv_format(handle) != fmt:
             raise RuntimeError("library reports another page format than requested")
+        if self._lib.vk_pool_page_bytes(handle) != self.page_bytes:
+            raise RuntimeError("library reports %d bytes per page, expected %d"
+                               % (self._lib.vk_pool_page_bytes(handle), self.page_bytes))
         self.handle = handle
         self._ws = None
 
