@@ -78,3 +78,23 @@ def test_product_does_not_reference_oracle():
 def test_build_flags_target_sm100a():
     from vulcan_b200 import build
     assert "arch=compute_100a,code=sm_100a" in build.NVCC_FLAGS
+
+
+def test_fp8_pool_argument_checks():
+    """vk_pool_create_fmt rejects bad formats and shapes on the host, before any
+    device call: an unknown format, FP8 with head_dim other than 128 or pages of
+    other than 16 tokens, and a byte-page pool with a format."""
+    lib = _lib.load()
+    handle = ctypes.c_void_p()
+    cfg = _lib.VkPoolCfg(1, 1, 128, 16, 4, 0, 0)
+    assert lib.vk_pool_create_fmt(ctypes.byref(cfg), 7, None, 0, ctypes.byref(handle)) == _lib.VK_INVALID_ARG
+    assert b"kv_format" in lib.vk_last_error_string()
+    cfg64 = _lib.VkPoolCfg(1, 1, 64, 16, 4, 0, 0)
+    assert lib.vk_pool_create_fmt(ctypes.byref(cfg64), 1, None, 0, ctypes.byref(handle)) == _lib.VK_UNSUPPORTED
+    cfg8 = _lib.VkPoolCfg(1, 1, 128, 8, 4, 0, 0)
+    assert lib.vk_pool_create_fmt(ctypes.byref(cfg8), 1, None, 0, ctypes.byref(handle)) == _lib.VK_UNSUPPORTED
+    raw = _lib.VkPoolCfg(0, 0, 0, 0, 4, 0, 4096)
+    assert lib.vk_pool_create_fmt(ctypes.byref(raw), 1, None, 0, ctypes.byref(handle)) == _lib.VK_INVALID_ARG
+    assert lib.vk_pool_create_fmt(ctypes.byref(cfg), 1, ctypes.c_void_p(0x1001), 1 << 30,
+                                  ctypes.byref(handle)) == _lib.VK_INVALID_ARG  # misaligned caller memory
+    assert lib.vk_pool_kv_format(None) == -1
