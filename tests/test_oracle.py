@@ -307,3 +307,29 @@ def test_fp8_append_dequant_round_trip():
     untouched = [p for p in range(g.num_pages) if p not in (3, 1)]
     assert np.array_equal(pool[:, untouched], before[:, untouched])
     assert np.array_equal(pool[0], before[0])
+
+
+def test_fp8_oracle_prefill_last_row_is_decode():
+    """The FP8 oracle's prefill and decode agree: the last row of a chunk that
+    ends a sequence is that sequence's decode row (same keys, same query)."""
+    rng = np.random.default_rng(94)
+    Hq, Hkv, D, T = 4, 2, 128, 21
+    pos = np.array([0, 37, 250], np.int32)
+    lens = pos + T
+    g = oracle.Geom(1, Hkv, D, 16, int(((lens + 15) // 16).sum()) + 2)
+    perm = rng.permutation(g.num_pages).astype(np.int32)
+    width = int(((lens + 15) // 16).max())
+    bt = np.full((len(lens), width), -1, np.int32)
+    off = 0
+    for b, n in enumerate(lens):
+        k = (n + 15) // 16
+        bt[b, :k] = perm[off:off + k]
+        off += k
+    pool = np.zeros((1, g.num_pages, Hkv, oracle.fp8_block_bytes(D)), np.uint8)
+    for b, n in enumerate(lens):
+        kv = (rng.standard_normal((2, 1, n, Hkv, D)) * 0.5).astype(np.float32)
+        assert oracle.append_fp8(pool, g, 0, kv[0], kv[1], bt[b:b + 1], np.zeros(1, np.int32)) == 0
+    q = (rng.standard_normal((len(lens), T, Hq, D)) * 0.5).astype(np.float32)
+    pre = oracle.prefill_fp8(pool, g, 0, q, bt, pos)
+    dec = oracle.decode_fp8(pool, g, 0, q[:, -1], bt, lens)
+    assert np.allclose(pre[:, -1], dec, rtol=1e-12, atol=1e-12)
