@@ -305,6 +305,8 @@ def main():
     if args.config == "prefill":
         return run_prefill(args, wl)
     if args.config == "churn":
+        if args.kv != "fp16":
+            raise SystemExit("--kv fp8 applies to the decode configs (70b, 7b) and prefill, not churn")
         return run_churn(args, wl)
 
     import torch
