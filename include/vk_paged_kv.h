@@ -227,7 +227,10 @@ vk_status vk_decode_plan_set_early_start(vk_decode_plan* plan, int32_t enable);
 vk_status vk_set_decode_workers(vk_pool* pool, int32_t max_workers);
 
 /* Plan facts: 0 workers, 1 CTAs, 2 partial slots, 3 total pages, 4 longest
- * sequence in pages; -1 for an unknown query. */
+ * sequence in pages, 5 most pieces of a unit that its last piece merges (1:
+ * every split unit is merged by dealt tasks), 6 units merged by their last
+ * piece, 7 units merged by dealt tasks, 8 most pieces of any unit, 9 merge
+ * tasks; -1 for an unknown query. */
 int32_t   vk_decode_plan_info(const vk_decode_plan* plan, int32_t what);
 vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer, const void* q,
                         void* out, const int32_t* block_tables, int32_t bt_stride,
@@ -270,7 +273,8 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
  * the gathered output; with wait_prev = 0 the gather of layer l overlaps layer l+1
  * (the order of an all-gather on a side stream).  Waits are bounded (1 s) and
  * record VK_ERR_TIMEOUT (vk_pool_check for runs, vk_gather_check for
- * vk_decode_plan_gather_wait).  The library does not order a slot's reuse
+ * vk_decode_plan_gather_wait); until that check clears it, later waits that
+ * record into the same error word give up at once.  The library does not order a slot's reuse
  * against the readers of a receive buffer: callers rewrite a slot only after a
  * wait that follows its readers on every rank (for example slot_base 0 and L
  * on alternate steps of L layers, with 2L slots).  No reference counterpart:
@@ -288,6 +292,12 @@ vk_status vk_gather_release_peers(vk_gather* g);
 vk_status vk_gather_destroy(vk_gather* g);
 vk_status vk_gather_export(const vk_gather* g, void* handle_out);
 vk_status vk_gather_import(vk_gather* g, int32_t peer, const void* handle);
+/* For a host that drives several ranks from one process (CUDA IPC cannot map
+ * a buffer into the process that allocated it): rank `peer` is the gather
+ * `peer_gather` of this process, on this device or another one with peer
+ * access (enabled here).  Both must have the same world, slots and
+ * slice_bytes, and peer_gather must be rank `peer`. */
+vk_status vk_gather_import_local(vk_gather* g, int32_t peer, const vk_gather* peer_gather);
 /* This rank's receive buffer of one slot: [world][slice_bytes] (NULL if bad). */
 void*     vk_gather_buffer(const vk_gather* g, int32_t slot);
 /* Synchronous: VK_TIMEOUT if a vk_decode_plan_gather_wait gave up since the
@@ -390,12 +400,17 @@ vk_status vk_attention_f32(const float* Q, const float* K, const float* V, float
  *
  * Limit: the shape must need at most VK_DECODE_STATIC_SCRATCH_BYTES of scratch
  * (vk_decode_workspace_size() for the same arguments); larger shapes return
- * VK_INVALID_ARG with a message, and nothing is launched.  Every GPU that
- * uses this entry point holds the array until the process exits.
+ * VK_INVALID_ARG with a message, and nothing is launched.  The array is part
+ * of the library's device code: under CUDA's default lazy module loading a
+ * GPU holds it from this entry point's first call there until the process
+ * exits; with CUDA_MODULE_LOADING=EAGER every GPU on which the process creates
+ * a context holds it, whether it calls this entry point or not.
  *
  * The first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any stream
- * capture.  All calls on a device share the one array and it keeps the last
+ * device, with that device current) and keeps it for the life of the
+ * process; make that first call before any stream capture.  After
+ * cudaDeviceReset on a device (which unloads the library's device code there)
+ * do not call this entry point on that device again.  All calls on a device share the one array and it keeps the last
  * call's contents; nothing in it needs to start at zero, because every split
  * writes its partial result before the merge reads it.  Calls that overlap on
  * the GPU (different streams, or concurrent host threads) race on the array:

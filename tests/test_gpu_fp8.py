@@ -249,3 +249,84 @@ def test_fp8_unsupported_entry_points(vk):
         pool.kv_view()
     with pytest.raises(vk.VKError):
         vk.PagedKVPool(1, 1, 64, 4, kv_format="fp8")
+
+
+def test_fp8_last_piece_merge(vk):
+    """FP8 pages on the long-worker-range path of the planned decode (>= 64
+    pages per worker): units of 2..8 pieces merged by their last piece next to
+    a unit of more than 8 pieces merged by tasks; fused append bit-exact;
+    repeated runs bit-identical."""
+    rng = np.random.default_rng(860)
+    Hkv, D, L, layer, G = 2, 128, 1, 0, 8
+    Hq = G * Hkv
+    lens = np.array([16000, 4000, 1600, 2600, 300, 17, 1, 6000], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool, host = fp8_pool(vk, g, rng)
+    fill_history(vk, pool, host, g, rng, layer, bt, lens)
+    pool.set_plan_workers(16 * Hkv)
+    plan = pool.plan(lens.tolist(), Hq)
+    pool.set_plan_workers(0)
+    assert plan.info(3) // plan.workers >= 64 and plan.info(5) == 8
+    assert plan.info(6) >= 3 and plan.info(7) >= 1 and plan.info(8) > 8
+    B = len(lens)
+    q = rows(rng, B, Hq, D)
+    kn, vn = rows(rng, B, Hkv, D), rows(rng, B, Hkv, D)
+    qd, btd = dev_f16(q), dev_i32(bt)
+    out = plan.run(layer, qd, btd, k_new=dev_f16(kn), v_new=dev_f16(vn))
+    again = [plan.run(layer, qd, btd).clone() for _ in range(2)]
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert torch.equal(again[0], again[1])
+    assert oracle.append_fp8(host, g, layer, kn[:, None], vn[:, None], bt, lens - 1) == 0
+    assert_bytes(pool, host, "FP8 fused append (last-piece merge plan)")
+    ref = oracle.decode_fp8(host, g, layer, q, bt, lens)
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 last-piece merge")
+    assert_close_attn(again[0].float().cpu().numpy(), ref, "FP8 last-piece merge, rerun")
+
+
+def test_fp8_70b_full_layer_fused_append(vk):
+    """A full Llama-2-70B GQA layer on FP8 pages (B=64, 64/8 heads, lognormal
+    contexts median 2048 clipped to [256, 8192]), default workers, history
+    written by the quantising append, new token by the fused append; sampled sequences (longest, shortest, six more) checked
+    against the oracle: block bytes bit-exact, outputs within tolerance."""
+    rng = np.random.default_rng(870)
+    B, Hq, Hkv, D, L, layer = 64, 64, 8, 128, 1, 0
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(2048), 0.6, B))), 256, 8192).astype(np.int32) + 1
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool = vk.PagedKVPool(L, Hkv, D, g.num_pages, kv_format="fp8")
+    blocks = pool.block_view()
+    blocks.zero_()
+    gen = torch.Generator("cuda").manual_seed(3)
+    btd = dev_i32(bt)
+    for b, n in enumerate(lens):
+        kh = (torch.randn((1, int(n) - 1, Hkv, D), device="cuda", generator=gen) * 0.5).half()
+        vh = (torch.randn((1, int(n) - 1, Hkv, D), device="cuda", generator=gen) * 0.5).half()
+        pool.append(layer, kh, vh, btd[b:b + 1], dev_i32([0]))
+    plan = pool.plan(lens.tolist(), Hq)
+    # FP8 runs more resident warps than fp16 (6 CTAs per SM), so this layer has
+    # ~40 pages per worker and its split units are merged by dealt tasks
+    assert plan.info(5) == (8 if plan.info(3) // plan.workers >= 64 else 1)
+    assert plan.info(7) > 0 or plan.info(6) > 0
+    sample = [int(np.argmax(lens)), int(np.argmin(lens))] + [int(x) for x in rng.choice(B, 6, replace=False)]
+    pages, tabs = [], np.full((len(sample), bt.shape[1]), -1, np.int32)
+    for i, b in enumerate(sample):
+        n = (int(lens[b]) + 15) // 16
+        tabs[i, :n] = np.arange(len(pages), len(pages) + n, dtype=np.int32)
+        pages.extend(int(x) for x in bt[b, :n])
+    idx = torch.tensor(pages, dtype=torch.long, device="cuda")
+    before = blocks.index_select(1, idx).cpu().numpy()
+    q = rows(rng, B, Hq, D)
+    kn, vn = rows(rng, B, Hkv, D), rows(rng, B, Hkv, D)
+    out = plan.run(layer, dev_f16(q), btd, k_new=dev_f16(kn), v_new=dev_f16(vn))
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    after = blocks.index_select(1, idx).cpu().numpy()
+    gs = oracle.Geom(L, Hkv, D, 16, len(pages))
+    expect = np.ascontiguousarray(before)
+    assert oracle.append_fp8(expect, gs, layer, kn[sample][:, None], vn[sample][:, None], tabs, lens[sample] - 1) == 0
+    bad = after != expect
+    assert not bad.any(), "FP8 fused append, sampled sequences: %d bytes differ" % int(bad.sum())
+    ref = oracle.decode_fp8(expect, gs, layer, q[sample], tabs, lens[sample])
+    assert_close_attn(out.float().cpu().numpy()[sample], ref, "FP8 70B full layer, sampled")

@@ -155,3 +155,172 @@ def test_planned_fused_gather_one_rank(vk):
     gat.check()
     assert pool.check() == 0
     gat.close()
+
+
+# Lengths (tokens) whose units, with 16 workers per KV head, give ~120 pages
+# per worker: a 1000-page unit of more than 8 pieces (merged by dealt tasks)
+# next to units of 2..4 pieces (merged by their last piece), single-piece
+# units, a one-token unit and an empty one.
+_LMM_LENS = np.array([16000, 4000, 1600, 2600, 300, 17, 1, 6000, 0], np.int32)
+
+
+def _lmm_plan(pool, lens, Hq, Hkv):
+    pool.set_plan_workers(16 * Hkv)
+    plan = pool.plan(lens.tolist(), Hq)
+    pool.set_plan_workers(0)
+    assert plan.info(3) // plan.workers >= 64, "the case must have long worker ranges"
+    assert plan.info(5) == 8, "units of up to 8 pieces must merge in their last piece"
+    assert plan.info(6) >= 3, "several units merged by their last piece"
+    assert plan.info(7) >= 1 and plan.info(8) > 8, "one unit of more than 8 pieces merged by tasks"
+    return plan
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("Hq,Hkv", [(8, 1), (16, 1), (16, 2), (64, 8)])
+def test_planned_last_piece_merge(vk, D, Hq, Hkv):
+    """Long worker ranges (>= 64 pages each, the one-GPU 70B regime): units of
+    2..8 pieces are merged by whichever piece finishes last (acq_rel counter,
+    merge in head groups of 1024/D, counter reset by the merger), a unit of
+    more than 8 pieces by dealt tasks, in one plan.  Two rounds over two layers
+    on one uploaded plan are bit-identical (the counters reset themselves),
+    and the fused append lands bit-exact."""
+    if Hkv == 8 and D != 128:
+        pytest.skip("70B heads at D=128 only (pool size)")
+    rng = np.random.default_rng(400 + D + Hq + Hkv)
+    lens = _LMM_LENS
+    g, bt, host, q = _case(rng, lens, Hq, Hkv, D, L=2)
+    pool = make_pool(vk, g, host)
+    plan = _lmm_plan(pool, lens, Hq, Hkv)
+    qd, btd = dev_f16(q), dev_i32(bt)
+    first = [plan.run(l, qd, btd).clone() for l in range(2)]
+    for rep in range(2):
+        for l in range(2):
+            assert torch.equal(plan.run(l, qd, btd), first[l]), (rep, l)
+    assert pool.check() == 0
+    for l in range(2):
+        ref = oracle.decode_paged(host.view(np.uint16), g, l, q.view(np.uint16), bt, lens, nthreads=8)
+        assert_close_attn(first[l].float().cpu().numpy(), ref, "last-piece merge D%d Hq%d Hkv%d layer %d" % (D, Hq, Hkv, l))
+    # fused append on the same branch
+    B = len(lens)
+    k = (rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16)
+    v = (rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16)
+    out = plan.run(1, qd, btd, k_new=dev_f16(k), v_new=dev_f16(v)).float().cpu().numpy()
+    assert pool.check() == 0
+    has = lens > 0  # an empty sequence has no page to append into
+    expect = host.copy()
+    assert oracle.append_paged(expect.view(np.uint16), g, 1, k[has][:, None].view(np.uint16),
+                               v[has][:, None].view(np.uint16), bt[has], lens[has] - 1) == 0
+    got = pool.kv_view().cpu().numpy()
+    assert np.array_equal(got.view(np.uint16), expect.view(np.uint16)), "fused append (last-piece merge plan)"
+    ref = oracle.decode_paged(expect.view(np.uint16), g, 1, q.view(np.uint16), bt, lens, nthreads=8)
+    assert_close_attn(out[has], ref[has], "last-piece merge with fused append")
+
+
+def _compact(pool_dev, bt, sample, lens):
+    """The pages of the sampled sequences, gathered from a device pool view
+    [L, num_pages, ...] into a host array, and block tables renumbered to it."""
+    pages, tabs = [], np.full((len(sample), bt.shape[1]), -1, np.int32)
+    for i, b in enumerate(sample):
+        n = (int(lens[b]) + 15) // 16
+        tabs[i, :n] = np.arange(len(pages), len(pages) + n, dtype=np.int32)
+        pages.extend(int(x) for x in bt[b, :n])
+    idx = torch.tensor(pages, dtype=torch.long, device=pool_dev.device)
+    return pool_dev.index_select(1, idx).cpu().numpy(), tabs
+
+
+def _70b_lens(rng, B=64):
+    return np.clip(np.round(np.exp(rng.normal(np.log(2048), 0.6, B))), 256, 8192).astype(np.int32) + 1
+
+
+def test_planned_70b_full_layer_fused_append(vk):
+    """The headline configuration of one GPU: a full Llama-2-70B GQA layer (B=64,
+    64/8 heads, D=128, lognormal contexts median 2048 clipped to [256, 8192]),
+    default workers (one per resident warp), so ~80 pages per worker and the
+    last-piece merge path; fused append of the new token.  Two layers run back
+    to back with early start (programmatic dependent launch), as in the
+    benchmark step.  Sampled sequences (longest, shortest and six more) are
+    checked against the oracle: appended rows bit-exact, outputs within the
+    attention tolerance."""
+    rng = np.random.default_rng(700)
+    B, Hq, Hkv, D, L = 64, 64, 8, 128, 2
+    lens = _70b_lens(rng, B)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, lens)
+    pool = make_pool(vk, g)
+    kv = pool.kv_view()
+    kv.copy_((torch.randn(kv.shape, device="cuda", generator=torch.Generator("cuda").manual_seed(2)) * 0.5).half())
+    plan = pool.plan(lens.tolist(), Hq)
+    assert plan.info(5) == 8 and plan.info(6) > 0, "the 70B layer must take the last-piece merge path"
+    assert plan.info(3) // plan.workers >= 64
+    plan.set_early_start(True)
+    sample = [int(np.argmax(lens)), int(np.argmin(lens))] + [int(x) for x in rng.choice(B, 6, replace=False)]
+    before, tabs = _compact(kv, bt, sample, lens)
+    q = [(rng.standard_normal((B, Hq, D)) * 0.5).astype(np.float16) for _ in range(L)]
+    k = [(rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16) for _ in range(L)]
+    v = [(rng.standard_normal((B, Hkv, D)) * 0.5).astype(np.float16) for _ in range(L)]
+    btd = dev_i32(bt)
+    outs = [plan.run(l, dev_f16(q[l]), btd, k_new=dev_f16(k[l]), v_new=dev_f16(v[l])) for l in range(L)]
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    after, _ = _compact(kv, bt, sample, lens)
+    gs = oracle.Geom(L, Hkv, D, 16, before.shape[1])
+    expect = np.ascontiguousarray(before)
+    for l in range(L):
+        assert oracle.append_paged(expect.view(np.uint16), gs, l, k[l][sample][:, None].view(np.uint16),
+                                   v[l][sample][:, None].view(np.uint16), tabs, lens[sample] - 1) == 0
+    assert np.array_equal(after.view(np.uint16), expect.view(np.uint16)), "fused append, sampled sequences"
+    for l in range(L):
+        ref = oracle.decode_paged(expect.view(np.uint16), gs, l, q[l][sample].view(np.uint16), tabs, lens[sample],
+                                  nthreads=8)
+        assert_close_attn(outs[l].float().cpu().numpy()[sample], ref, "70B full layer %d, sampled" % l)
+
+
+def test_gather_wait_times_out_and_recovers(vk):
+    """Two ranks of a gather driven from this process on one GPU.  Rank 0's end
+    of step waits for rank 1's flag, which nothing raises: the bounded wait
+    gives up after about 1 s, the host reads VK_TIMEOUT (once; the check
+    clears it) and the device stays usable.  Rank 1's step then passes (its
+    wait finds rank 0's flag already raised), and both receive buffers hold
+    both ranks' outputs.  Only one kernel waits at a time, never on another
+    running kernel."""
+    import time
+    rng = np.random.default_rng(32)
+    lens = np.array([5, 300, 2049], np.int32)
+    Hq, Hkv, D = 16, 2, 128
+    g, bt, host, q0 = _case(rng, lens, Hq, Hkv, D, L=1)
+    q1 = (rng.standard_normal(q0.shape) * 0.5).astype(np.float16)
+    pool = make_pool(vk, g, host)
+    bt_d = dev_i32(bt)
+    B = len(lens)
+    want0 = pool.plan(lens.tolist(), Hq).run(0, dev_f16(q0), bt_d).clone()
+    want1 = pool.plan(lens.tolist(), Hq).run(0, dev_f16(q1), bt_d).clone()
+    nbytes = B * Hq * D * 2
+    g0, g1 = vk.Gather(0, 2, nbytes, slots=2), vk.Gather(1, 2, nbytes, slots=2)
+    g0.import_local(1, g1)
+    g1.import_local(0, g0)
+    plan0 = pool.plan(lens.tolist(), Hq)
+    plan0.set_gather(g0, slot_base=0, wait_prev=False)
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    plan0.run(0, dev_f16(q0), bt_d)
+    plan0.gather_wait(0)
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert 0.9 < waited < 10.0, "the wait must give up after its 1 s bound (took %.2f s)" % waited
+    with pytest.raises(vk.VKError) as e:
+        g0.check()
+    assert e.value.status == 4  # VK_TIMEOUT
+    g0.check()  # cleared by the first check
+    assert pool.check() == 0
+    plan1 = pool.plan(lens.tolist(), Hq)
+    plan1.set_gather(g1, slot_base=0, wait_prev=False)
+    plan1.run(0, dev_f16(q1), bt_d)
+    plan1.gather_wait(0)
+    torch.cuda.synchronize()
+    g1.check()
+    assert pool.check() == 0
+    for gat in (g0, g1):
+        got = gat.view(0, B, Hq, D)
+        assert torch.equal(got[0], want0) and torch.equal(got[1], want1)
+    g0.close()
+    g1.close()

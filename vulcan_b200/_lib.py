@@ -69,6 +69,7 @@ SIGNATURES = {
     "vk_gather_release_peers": (c_i32, [vp]),
     "vk_gather_export": (c_i32, [vp, vp]),
     "vk_gather_import": (c_i32, [vp, c_i32, vp]),
+    "vk_gather_import_local": (c_i32, [vp, c_i32, vp]),
     "vk_gather_buffer": (vp, [vp, c_i32]),
     "vk_decode_plan_gather_wait": (c_i32, [vp, vp, c_i32, vp]),
     "vk_gather_check": (c_i32, [vp]),

@@ -676,6 +676,7 @@ struct vk_decode_plan {
     mutable std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
     int ntasks = 0, S = 1, lmm = 1;
+    int last_merge_units = 0, max_pieces = 0;  // units merged by their last piece; most pieces of one unit
     size_t o_hdr = 0;  // [0]: step epoch written at upload (fused gather)
     size_t tables_bytes = 0, counters_off = 0, part_o_off = 0, part_lse_off = 0, ws_bytes = 0;
     bool early_start = false;
@@ -807,10 +808,12 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
         const int32_t f = worker_of(uoff[u]), l = worker_of(uoff[u + 1] - 1);
         ufw[u] = f;
         unp[u] = l - f + 1;
+        pl->max_pieces = std::max(pl->max_pieces, unp[u]);
         if (unp[u] > 1) {
             uslot[u] = slots;
             slots += unp[u];
             if (unp[u] > pl->lmm) tunits.push_back(u);  // merged by dealt tasks
+            else ++pl->last_merge_units;
         }
     }
     pl->slots = slots;
@@ -928,6 +931,11 @@ int32_t vk_decode_plan_info(const vk_decode_plan* plan, int32_t what) {
         case 2: return plan->slots;
         case 3: return plan->total_pages;
         case 4: return plan->max_unit_pages;
+        case 5: return plan->lmm;
+        case 6: return plan->last_merge_units;
+        case 7: return plan->ntasks / plan->S;
+        case 8: return plan->max_pieces;
+        case 9: return plan->ntasks;
         default: return -1;
     }
 }

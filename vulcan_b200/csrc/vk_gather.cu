@@ -17,6 +17,7 @@ struct vk_gather {
     char* own = nullptr;
     char* peer[vk::kMaxGatherRanks] = {};
     bool imported[vk::kMaxGatherRanks] = {};
+    bool local[vk::kMaxGatherRanks] = {};  // peer is a gather of this process (not an IPC mapping)
 };
 
 namespace vk {
@@ -90,9 +91,12 @@ vk_status vk_gather_release_peers(vk_gather* g) {
     cudaError_t e = cudaDeviceSynchronize();
     for (int r = 0; r < g->world; ++r)
         if (g->imported[r]) {
-            cudaError_t c = cudaIpcCloseMemHandle(g->peer[r]);
-            if (e == cudaSuccess) e = c;
+            if (!g->local[r]) {
+                cudaError_t c = cudaIpcCloseMemHandle(g->peer[r]);
+                if (e == cudaSuccess) e = c;
+            }
             g->imported[r] = false;
+            g->local[r] = false;
             g->peer[r] = nullptr;
         }
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "closing peer mappings");
@@ -131,6 +135,31 @@ vk_status vk_gather_import(vk_gather* g, int32_t peer, const void* handle) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
     g->peer[peer] = static_cast<char*>(p);
     g->imported[peer] = true;
+    return VK_OK;
+}
+
+vk_status vk_gather_import_local(vk_gather* g, int32_t peer, const vk_gather* pg) {
+    if (!g || !pg) return fail(VK_INVALID_ARG, "gather or peer gather is NULL");
+    if (peer < 0 || peer >= g->world || peer == g->rank) return fail(VK_INVALID_ARG, "peer outside [0, world) or own rank");
+    if (g->imported[peer]) return fail(VK_INVALID_ARG, "peer already imported");
+    if (pg->rank != peer || pg->world != g->world || pg->slots != g->slots || pg->slice_bytes != g->slice_bytes)
+        return fail(VK_INVALID_ARG, "peer gather has another rank, world, slot count or slice size");
+    if (pg->device != g->device) {
+        DeviceGuard dg(g->device);
+        int ok = 0;
+        cudaError_t e = cudaDeviceCanAccessPeer(&ok, g->device, pg->device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+        if (!ok) return fail(VK_UNSUPPORTED, "no peer access between the two devices");
+        e = cudaDeviceEnablePeerAccess(pg->device, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) {
+            cudaGetLastError();  // not an error here: drop it from the runtime's last-error state
+        } else if (e != cudaSuccess) {
+            return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+        }
+    }
+    g->peer[peer] = pg->own;
+    g->imported[peer] = true;
+    g->local[peer] = true;
     return VK_OK;
 }
 

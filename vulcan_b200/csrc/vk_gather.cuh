@@ -30,13 +30,15 @@ __device__ __forceinline__ uint32_t* gather_flag(const GatherView& g, int on_ran
 
 // One thread: waits until every rank's flag of `slot` in this rank's block has
 // reached `target` (flags carry step epochs and only grow, mod 2^32).  False,
-// with VK_ERR_TIMEOUT, after kGatherWaitNs.
+// with VK_ERR_TIMEOUT, after kGatherWaitNs, or at once when another wait on
+// the same error word has already given up (so a failed step costs one bound,
+// not one per waiting warp).
 __device__ __forceinline__ bool gather_wait_slot(const GatherView& g, int slot, uint32_t target, uint32_t* err) {
     const uint64_t t0 = global_ns();
     for (int r = 0; r < g.world; ++r) {
         const uint32_t* f = gather_flag(g, g.rank, slot, r);
         while (static_cast<int32_t>(ld_acquire_sys(f) - target) < 0) {
-            if (global_ns() - t0 > kGatherWaitNs) {
+            if ((*reinterpret_cast<volatile uint32_t*>(err) & VK_ERR_TIMEOUT) || global_ns() - t0 > kGatherWaitNs) {
                 atomicOr(err, VK_ERR_TIMEOUT);
                 return false;
             }

@@ -414,6 +414,12 @@ class Gather:
     def import_peer(self, peer: int, handle: bytes) -> None:
         buf = ctypes.create_string_buffer(bytes(handle), self.HANDLE_BYTES)
         check(self._lib.vk_gather_import(self.handle, peer, buf), "vk_gather_import")
+        self._ipc_peers = True
+
+    def import_local(self, peer: int, other: "Gather") -> None:
+        """Rank ``peer`` is ``other``, a gather of this process (one host
+        process driving several ranks; see vk_gather_import_local)."""
+        check(self._lib.vk_gather_import_local(self.handle, peer, other.handle), "vk_gather_import_local")
 
     def exchange(self, group=None) -> None:
         """Swaps handles with every rank through torch.distributed (host side)."""
@@ -445,12 +451,14 @@ class Gather:
 
     def close(self, group=None) -> None:
         """Two-phase teardown: release the peer mappings, meet every rank at a
-        torch.distributed barrier (when world > 1), then free the buffer."""
+        torch.distributed barrier (when peers were imported from other
+        processes), then free the buffer."""
         if getattr(self, "handle", None) is not None and self.handle.value:
             if self.world > 1:
-                import torch.distributed as dist
                 self.release_peers()
-                dist.barrier(group=group)
+                if getattr(self, "_ipc_peers", False):
+                    import torch.distributed as dist
+                    dist.barrier(group=group)
             self._lib.vk_gather_destroy(self.handle)
             self.handle = ctypes.c_void_p()
 
