@@ -1,23 +1,31 @@
 """Paged decode benchmark: KV append + paged GQA decode over every layer of one
 decode step, on 1..N B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 70b|7b]
-                    [--impl ours|reference] [--no-e2e] [--no-cpu-baseline]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 70b|7b|prefill|churn]
+                    [--impl ours|reference] [--kv fp16|fp8] [--gather p2p|p2p-wait|nccl]
+                    [--no-e2e] [--no-cpu-baseline]
 
 Workloads (synthetic, seeded; fp16 K/V/Q drawn from N(0, 0.5^2)):
   70b  Llama-2-70B-shaped GQA decode: 64 query heads, 8 KV heads, head dim 128,
        80 layers, batch 64, context lengths lognormal (median 2048, sigma 0.6)
        clipped to [256, 8192], 16-token pages in a random block table.  At N
        GPUs each rank holds 8/N KV heads (and their 64/N query heads) of every
-       sequence; the per-layer outputs are all-gathered with NCCL on a
-       communication stream that overlaps the next layer.
+       sequence; each layer's output is all-gathered inside the decode kernel
+       itself (peer stores into every rank's receive buffer over NVLink, one
+       flag per rank and layer; --gather nccl uses an NCCL all-gather on a side
+       stream instead).
   7b   Llama-2-7B decode: 32/32 heads, head dim 128, 32 layers, batch 32,
        contexts uniform in [128, 4096], pool 1.2x the tokens; sequences are
        sharded across ranks (no collective).
+  prefill, churn: chunked prefill and long-context paged churn (one GPU).
 
-One step = for every layer: append one token per sequence (K1), then decode
-attention over the whole context (K2: split-K decode + merge).  Timed with CUDA
-events between barriers, max over ranks.  Rank 0 prints one JSON line.
+One step = for every layer one planned-decode launch (vk_decode_run): the new
+token's K/V appended into its page, paged attention over the whole context with
+the split units merged in the same launch, and the gather when sharded; the
+host plan is built and uploaded once per step, and the layers run as one CUDA
+graph with programmatic dependent launch between them.  Timed with CUDA events
+between barriers, max over ranks.  Rank 0 prints one JSON line.  --impl
+reference times the reference's CPU attention (oracle port) on the host cores.
 """
 from __future__ import annotations
 
@@ -107,6 +115,17 @@ def algorithmic_bytes(ctx, Hq, Hkv, D, kv_format="fp16"):
     qo = len(ctx) * 2 * Hq * D * 2
     table = int((4 * ((lens + PAGE - 1) // PAGE)).sum())
     return dict(decode=kv + qo + table, append=new, total=kv + new + qo + table)
+
+
+def workload_config(wl, kv_format, world):
+    """The `config` object of both arms' JSON lines: what the workload is, not
+    how an arm runs it (that goes under `run`), so the two arms' lines carry
+    the same config at every N."""
+    ab = algorithmic_bytes(wl["ctx"], wl["Hq"], wl["Hkv"], wl["D"], kv_format)
+    return {"workload": wl["desc"], "kv_format": kv_format,
+            "shard": wl["shard"] if world > 1 else "none",
+            "l2": "inputs larger than L2: %.1f GB of K/V read per step" % (ab["decode"] * wl["L"] / 1e9),
+            "context_tokens": int((wl["ctx"] + 1).sum())}
 
 
 def fill_fp8(pool, D, dev, gen):
@@ -248,15 +267,25 @@ def run_reference_arm(args, wl):
         t = cpu_decode_sample(wl, bt, ctx, wl["Hkv"], wl["Hq"], seqs, threads)
         if i >= args.warmup:
             times.append(t)
-    per_layer = statistics.median(times) / frac
-    step_s = per_layer * wl["L"]
+    sample_s = statistics.median(times)
+    step_s = sample_s / frac * wl["L"]  # the whole step, extrapolated from the sample
     value = wl["B"] / step_s
-    sample = ("1 of %d layers, %d of %d sequences (all %d heads) per step; step time extrapolated "
-              "x%d layers / %.3f of the tokens" % (wl["L"], len(seqs), wl["B"], wl["Hq"], wl["L"], frac))
+    sample = ("1 of %d layers, %d of %d sequences (all %d heads) per step, %.2f s measured per sample; "
+              "tokens/s extrapolated x%d layers / %.3f of the tokens"
+              % (wl["L"], len(seqs), wl["B"], wl["Hq"], sample_s, wl["L"], frac))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "steps": args.steps, "warmup": args.warmup,
+            # what was timed: one bounded sample per step (the full step would
+            # take ms_per_step_extrapolated)
+            "ms_per_step": sample_s * 1e3, "ms_per_step_kind": "measured sample (see extrapolated)",
+            "extrapolated": {"layers": wl["L"], "token_frac": frac, "sample_ms": sample_s * 1e3,
+                             "ms_per_step_extrapolated": step_s * 1e3,
+                             "value_is": "B / ms_per_step_extrapolated"},
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": wl["desc"], "shard": wl["shard"]},
+            "data": "synthetic (seeded N(0,0.5^2) fp16 K/V/Q, random block tables)",
+            "config": workload_config(wl, args.kv, args.gpus),
+            "run": {"threads": threads, "code": "oracle port of the reference's golden cpu_attention "
+                                                 "(decode row over the paged gather)"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -536,8 +565,8 @@ def main():
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f16" if args.kv == "fp16" else "e4m3 K/V pages (fp32 scale per 128-value row), f16 Q/O, f32 accumulation",
             "data": "synthetic (seeded N(0,0.5^2) fp16 K/V/Q, random block tables)",
-            "config": {"workload": wl["desc"], "kv_format": args.kv, "shard": wl["shard"] if world > 1 else "none",
-                       "parallelism": ("kv-head shard x%d + %s" % (world, "allgather fused into the decode "
+            "config": workload_config(wl, args.kv, world),
+            "run": {"parallelism": ("kv-head shard x%d + %s" % (world, "allgather fused into the decode "
                                                                       "(peer stores over NVLink, flag per layer)"
                                                                       + (", each layer waits for the previous "
                                                                          "layer's gather" if args.gather == "p2p-wait"
@@ -545,12 +574,10 @@ def main():
                                                                       if gat is not None else "NCCL allgather")
                                        if wl["shard"] == "head" else "sequence shard x%d" % world)
                                       if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2: %.1f GB of K/V read per step" % (ab_job["decode"] * L / 1e9),
                        "decode_path": args.path,
                        "launch": "CUDA graph of the %d-layer step" % L if use_graph else "eager",
                        "pages_per_split": pool.pages_per_split(Bl, max_len) if args.path == "split" else None,
-                       "plan_workers": pool.plan(lens_host, hq_l).workers if args.path == "planned" else None,
-                       "context_tokens": int((ctx_all + 1).sum())},
+                       "plan_workers": pool.plan(lens_host, hq_l).workers if args.path == "planned" else None},
             "hbm_gbs": job_gbs / world,
             "hbm_frac_of_peak": job_gbs / world / peak,
             "gpu_launches": launches_per_step * args.steps,
@@ -838,11 +865,10 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     """Same step through the public API with host buffers: each layer's q/k/v is
     copied from pinned host memory to the device on a copy stream (double
     buffered, overlapping the previous layer's kernel; they stand in for the
-    projections a model computes on the device), and the step's result, the
-    last layer's (all-gathered) attention output, is copied back to pinned host
-    memory on a second copy stream, all inside the timed region.  Earlier
-    layers' outputs stay on the device, as in a model where they feed the next
-    layer.  At N=1 the step is one CUDA graph."""
+    projections a model computes on the device), and every layer's attention
+    output (this rank's heads) is copied back to pinned host memory on a second
+    copy stream, plus the last layer's all-gathered output when heads are
+    sharded, all inside the timed region.  At N=1 the step is one CUDA graph."""
     import torch
     import torch.distributed as dist
     g = torch.Generator()
@@ -853,6 +879,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     gathered_host = gathered is not None or gat is not None
     out_shape = (world, Bl, hq_l, D) if gathered_host else (Bl, hq_l, D)
     hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
+    hout_layers = torch.empty(L, Bl, hq_l, D, dtype=torch.float16).pin_memory()  # every layer, own heads
     nbuf = 2
     dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
     dk = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
@@ -862,7 +889,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     d2h = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
     h2d_bytes = (hq.numel() + hk.numel() + hv.numel()) * 2
-    d2h_bytes = hout.numel() * 2
+    d2h_bytes = hout_layers.numel() * 2 + (hout.numel() * 2 if gathered_host else 0)
     plan_keep = {}
 
     def new_plan(parity=0):
@@ -915,31 +942,33 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             freed[s] = fe
             last = l == L - 1
             if gat is not None:
-                if last:
-                    # the copy stream waits for every rank's slices of the last
-                    # layer (ranks raise their flags in layer order, so this
-                    # covers the step), then reads the slot
-                    d2h.wait_event(fe)
-                    with torch.cuda.stream(d2h):
+                # this rank's own slice of the layer's slot (written by its run)
+                d2h.wait_event(fe)
+                with torch.cuda.stream(d2h):
+                    hout_layers[l].copy_(gat.view(base + l, Bl, hq_l, D)[gat.rank], non_blocking=True)
+                    if last:
+                        # wait for every rank's slices of the last layer (ranks
+                        # raise their flags in layer order, so this covers the
+                        # step), then read the whole slot
                         plan.gather_wait(l, stream=d2h)
                         hout.copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
-            elif gathered_host:
-                comm.wait_event(fe)
-                with torch.cuda.stream(comm):
-                    dist.all_gather_into_tensor(gathered[l].view(-1), douts[s].view(-1))
-                    ge = torch.cuda.Event()
-                    ge.record(comm)
-                d2h.wait_event(ge)
-                src = gathered[l]
             else:
-                d2h.wait_event(fe)
-                src = douts[s]
-            if gat is None and last:
+                if gathered_host:
+                    comm.wait_event(fe)
+                    with torch.cuda.stream(comm):
+                        dist.all_gather_into_tensor(gathered[l].view(-1), douts[s].view(-1))
+                        ge = torch.cuda.Event()
+                        ge.record(comm)
+                    d2h.wait_event(ge)  # the all-gather has read douts[s]
+                else:
+                    d2h.wait_event(fe)
                 with torch.cuda.stream(d2h):
-                    hout.copy_(src, non_blocking=True)
+                    hout_layers[l].copy_(douts[s], non_blocking=True)
+                    if gathered_host and last:
+                        hout.copy_(gathered[l], non_blocking=True)
                     od = torch.cuda.Event()
                     od.record(d2h)
-                    outdone[s] = od
+                    outdone[s] = od  # douts[s] may be rewritten after this
         cur.wait_stream(d2h)
         cur.wait_stream(h2d)
 
@@ -998,9 +1027,11 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     del graph, graphs
     return {"ms_step": ms / args.steps, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d_bytes),
             "d2h_bytes_per_step": int(d2h_bytes),
-            "path": "PagedKVPool / DecodePlan (C ABI): every layer's q, k, v from pinned host memory, the "
-                    "step's result (last layer's gathered output) back to pinned host memory; H2D and D2H on "
-                    "copy streams inside the timed region" + ("; CUDA graph per step" if use_graph else "")}
+            "path": "PagedKVPool / DecodePlan (C ABI): every layer's q, k, v from pinned host memory; every "
+                    "layer's attention output (this rank's heads) back to pinned host memory" +
+                    (", and the last layer's all-gathered output" if gathered_host else "") +
+                    "; H2D and D2H on copy streams inside the timed region" +
+                    ("; CUDA graph per step" if use_graph else "")}
 
 
 if __name__ == "__main__":
