@@ -3,12 +3,18 @@
 // vulcan::KVCache over the B200 paged KV-cache library (libvulcan_kv.so).
 //
 // Same class name, constructor, methods and move-only semantics as VULCAN's
-// include/vulcan/kv_cache.h:34-92, so the engine compiles against it unchanged.
+// include/vulcan/kv_cache.h:34-92, so code using the class compiles against it.
 // Storage differs: the cache is a paged fp16 pool (16-token pages, taken on
 // demand by append) instead of contiguous fp32 [heads, max_seq, head_dim]
-// buffers.  append() still takes fp32 rows and rounds them to fp16.  The paged
-// additions (decode, block_table) replace the per-head launch_attention loop of
-// the reference engine (src/transformer.cpp:157-189).
+// buffers.  append() still takes fp32 rows and rounds them to fp16.
+//
+// What changes for the engine: get() no longer hands out contiguous fp32
+// [num_kv_heads, max_seq_len, head_dim] arrays, so the reference's
+// self_attention loop that strides them that way and calls launch_attention
+// per head (src/transformer.cpp:142, 157-189) must not be kept: it would read
+// paged fp16 bytes as fp32.  Replace that loop by decode() below (one
+// sequence) or by vulcan::PagedAttention (include/vulcan/paged_attention.h,
+// many sequences, one launch per layer).
 
 #include <cstddef>
 #include <cstdint>
@@ -41,7 +47,9 @@ public:
     /// Device addresses of layer `layer`'s K and V blocks of physical page 0.
     /// The pool is paged fp16: element (page, head, slot, d) of the layer is at
     /// k + (page*num_kv_heads + head)*2*16*head_dim*2 bytes + (slot*head_dim + d)*2
-    /// (V: the same offsets from v).  nullptr for a bad layer.
+    /// (V: the same offsets from v).  nullptr for a bad layer.  Unlike the
+    /// reference, these are not fp32 [num_kv_heads, max_seq_len, head_dim]
+    /// arrays: attention over the cache goes through decode() or the C ABI.
     void get(int layer, const float** k_out, const float** v_out) const;
 
     int current_length() const;
