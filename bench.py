@@ -77,6 +77,11 @@ def workload(name: str):
                     desc="Long-context paged churn, Llama-2-7B head shapes (32/32, D=128), 1 layer: 256 "
                          "sequences arriving Poisson(16)/step, contexts U[1k, 32k], pool 70% of demand, "
                          "LRU swap to pinned host and back, compaction by page copy every 25 steps, 200 decode steps")
+    if name == "70b-wo":
+        wl = workload("70b")
+        wl["desc"] = wl["desc"] + "; then wo (8192 x 8192 fp16 per layer) fused with its reduce-scatter"
+        wl["name"] = "llama2-70b-gqa-decode-wo"
+        return wl
     if name == "7b":
         rng = np.random.Generator(np.random.PCG64(4096))
         B = 32
@@ -299,7 +304,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="70b", choices=["70b", "7b", "prefill", "churn"])
+    ap.add_argument("--config", default="70b", choices=["70b", "7b", "prefill", "churn", "70b-wo"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -318,6 +323,8 @@ def main():
                     help="page format of the decode configs: fp16, or e4m3 codes with an fp32 scale per row")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: use only this many layers")
     ap.add_argument("--batch", type=int, default=0, help="profiling aid: use only the first B sequences")
+    ap.add_argument("--share-of", type=int, default=0,
+                    help="profiling aid: run rank 0's KV-head share of an N-GPU run alone on one GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -325,6 +332,8 @@ def main():
     if args.layers:
         wl["L"] = args.layers
         wl["desc"] += " [profiling case: %d layers]" % args.layers
+    if args.share_of > 1:
+        wl["desc"] += " [profiling case: rank 0's KV-head share of %d GPUs, alone on one GPU]" % args.share_of
     if args.batch:
         wl["B"] = args.batch
         wl["ctx"] = wl["ctx"][:args.batch]
@@ -333,6 +342,8 @@ def main():
         return run_reference_arm(args, wl)
     if args.config == "prefill":
         return run_prefill(args, wl)
+    if args.config == "70b-wo":
+        return run_attn_wo(args, wl)
     if args.config == "churn":
         if args.kv != "fp16":
             raise SystemExit("--kv fp8 applies to the decode configs (70b, 7b) and prefill, not churn")
@@ -359,7 +370,7 @@ def main():
     bt_all, num_pages_all = layout(ctx_all, wl["seed"])
     from vulcan_b200.shard import head_shard, seq_shard
     if wl["shard"] == "head":
-        sh = head_shard(Hkv, Hq, world, rank)
+        sh = head_shard(Hkv, Hq, args.share_of if (args.share_of > 1 and world == 1) else world, rank)
         hkv_l, hq_l = sh.num_kv_heads, sh.num_q_heads
         seqs = np.arange(B)
         ctx, bt, num_pages = ctx_all, bt_all, num_pages_all
@@ -742,6 +753,141 @@ def prefill_flops(ctx, T, Hq, D):
     the causal (query, key) pairs of each chunk (prefix keys + lower triangle)."""
     pairs = sum(int(T * c + T * (T + 1) // 2) for c in ctx)
     return 4 * D * Hq * pairs
+
+
+def run_attn_wo(args, wl):
+    """Attention + output projection of the 70B decode step (row 8f.3): per layer
+    the planned decode of this rank's KV heads (fused append), then the wo
+    projection of its attention output fused with the reduce-scatter over output
+    features (vk_oproj: tcgen05 GEMM tile by tile, partials stored into the
+    owning rank over NVLink).  Eager launches (the projection is a cooperative
+    launch); a second pass times the projection launches alone for its
+    roofline: weights + x + y through HBM, and the partials that cross NVLink."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    import vulcan_b200 as vk
+    from vulcan_b200.shard import head_shard
+    B, Hq, Hkv, D, L = wl["B"], wl["Hq"], wl["Hkv"], wl["D"], wl["L"]
+    hidden = Hq * D
+    ctx = wl["ctx"]
+    bt, num_pages = layout(ctx, wl["seed"])
+    sh = head_shard(Hkv, Hq, world, rank)
+    hkv_l, hq_l = sh.num_kv_heads, sh.num_q_heads
+    k_local = hq_l * D
+    lens = (ctx + 1).astype(np.int32)
+    pool = vk.PagedKVPool(L, hkv_l, D, num_pages, own_memory=False, zero=False)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    flat = pool.storage.view(torch.float16)
+    for s0 in range(0, flat.numel(), 1 << 28):
+        part = flat[s0:s0 + (1 << 28)]
+        part.copy_(torch.randn(part.shape, device=dev, generator=gen) * 0.5)
+    bt_d = torch.from_numpy(bt).to(dev)
+    q = (torch.randn(L, B, hq_l, D, device=dev, generator=gen) * 0.5).half()
+    kn = (torch.randn(L, B, hkv_l, D, device=dev, generator=gen) * 0.5).half()
+    vn = (torch.randn(L, B, hkv_l, D, device=dev, generator=gen) * 0.5).half()
+    w_t = torch.empty(L, hidden, k_local, device=dev, dtype=torch.float16)  # this rank's rows of wo, transposed
+    for l in range(L):
+        w_t[l].copy_(torch.randn(hidden, k_local, device=dev, generator=gen) * 0.02)
+    att = torch.empty(L, B, hq_l, D, device=dev, dtype=torch.float16)
+    y = torch.empty(L, B, hidden // world, device=dev, dtype=torch.float16)
+    op = vk.OutputProjection(rank, world, B, k_local, hidden, device=dev)
+    if world > 1:
+        op.exchange()
+    lens_host = lens.tolist()
+    plan_ws = torch.empty(pool.plan(lens_host, hq_l).workspace.numel() + 4096, dtype=torch.uint8, device=dev)
+    keep = {}
+
+    def step(ev=None):
+        p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+        p_.set_early_start(True)
+        p_.upload()
+        keep["plan"] = p_
+        cur = torch.cuda.current_stream(dev)
+        for l in range(L):
+            p_.run(l, q[l], bt_d, out=att[l], k_new=kn[l], v_new=vn[l])
+            if ev is not None:
+                ev[l][0].record(cur)
+            op.run(att[l].view(B, k_local), w_t[l], y=y[l])
+            if ev is not None:
+                ev[l][1].record(cur)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    op.check()
+    pool.check()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    clocks = clk.summary()
+    # the projection alone: events around each launch (one more step)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    barrier()
+    step(ev)
+    barrier()
+    op_ms = statistics.mean(ev[l][0].elapsed_time(ev[l][1]) for l in range(L))
+    op.check()
+    pool.check()
+    if world > 1:
+        t = torch.tensor([ms, op_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, op_ms = float(t[0]), float(t[1])
+    hbm_peak, peak_kind = measured_peaks()
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if peak_kind == "measured" else {}
+    tflops_peak = float(peaks.get("bf16_tflops", 1590.0))
+    hbm_b = hidden * k_local * 2 + B * k_local * 2 + B * (hidden // world) * 2  # weights + x + y
+    nvl_b = B * hidden * 4 * (world - 1) // world  # fp32 partials leaving this rank
+    flops = 2.0 * B * k_local * hidden
+    t_hbm = hbm_b / (hbm_peak * 1e9)
+    t_tc = flops / (tflops_peak * 1e12)
+    t_nvl = nvl_b / 770e9
+    target = max(t_hbm, t_tc, t_nvl)
+    bound = "hbm" if target == t_hbm else ("tensor" if target == t_tc else "nvlink")
+    ab = algorithmic_bytes(ctx, hq_l, hkv_l, D)
+    if rank == 0:
+        line = {"metric": "attention + wo step tokens/s (70B decode, head-sharded, wo fused with its reduce-scatter)",
+                "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f16 (fp32 accumulation, fp32 partial sums)",
+                "data": "synthetic (seeded N(0,0.5^2) K/V/Q, wo ~ N(0, 0.02^2))",
+                "config": workload_config(wl, "fp16", world),
+                "run": {"launch": "eager: per layer vk_decode_run (early start) + vk_oproj_run (cooperative)",
+                        "oproj_splits": op.splits, "oproj_ctas": (hidden // 128) * op.splits},
+                "per_layer_us": ms * 1e3 / L,
+                "step_hbm_gbs": (ab["total"] + hbm_b) * L / (ms * 1e-3) / 1e9,
+                "gpu_launches": 2 * L * args.steps, "clocks": clocks,
+                "roofline": {"kernel": "oproj_kernel (tcgen05 GEMM + reduce-scatter over NVLink)",
+                             "bound": bound, "launch_us": op_ms * 1e3,
+                             "target_us": target * 1e6, "frac": target / (op_ms * 1e-3),
+                             "hbm_bytes": hbm_b, "hbm_gbs": hbm_b / (op_ms * 1e-3) / 1e9, "hbm_peak": hbm_peak,
+                             "nvlink_bytes_out": nvl_b, "flops": flops, "tensor_tflops": flops / (op_ms * 1e-3) / 1e12,
+                             "peak_source": peak_kind + " (NVLink: 770 GB/s measured peer copy)"}}
+        print(json.dumps(line), flush=True)
+    op.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_prefill(args, wl):

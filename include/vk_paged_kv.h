@@ -310,6 +310,49 @@ vk_status vk_decode_plan_set_gather(vk_decode_plan* plan, vk_gather* g, int32_t 
 vk_status vk_decode_plan_gather_wait(const vk_decode_plan* plan, void* workspace, int32_t layer,
                                      void* stream);
 
+/* ---- output projection fused with its reduce-scatter -----------------------
+ * The `wo` matmul after attention (reference src/transformer.cpp:191-194:
+ * launch_matmul(attn_output, wo, output, T, hidden, hidden), cuda/matmul.cu:42-103,
+ * C = A * B) for KV-head sharding over `world` GPUs.  Rank r holds x_r, the
+ * attention output of its heads ([tokens, k_local] fp16: the [B, Hq/world, D]
+ * decode output), and the same rows of wo; y = sum_r x_r * wo[rows of r].  A
+ * run leaves on rank r the output features [r*n_out/world, (r+1)*n_out/world)
+ * of y ([tokens, n_out/world] fp16, row stride ldy): a reduce-scatter over
+ * features in the same launch as the tcgen05 GEMM, partial tiles stored into
+ * their owner's memory over NVLink as they finish (no NCCL call).  fp16 inputs,
+ * fp32 accumulation and fp32 partial sums, summed in rank order.
+ *
+ * Weights: w_t is this rank's rows of wo transposed, [n_out, k_local] fp16 with
+ * row stride ldw (an nn.Linear [out, in] weight's column slice).
+ * vk_oproj_pack_weight converts the reference's fp32 wo rows ([k_rows, n],
+ * row stride ldw) into that layout.
+ *
+ * Setup mirrors the gather (vk_gather_*): create on every rank with the same
+ * world, max_tokens, k_local and n_out; export / import the handles (or
+ * import_local for ranks driven by one process).  Every rank makes the same
+ * sequence of runs on one stream; runs wait for one another across ranks
+ * (bounded, 1 s; vk_oproj_check reports VK_TIMEOUT), so all ranks must run.
+ * Limits: max_tokens <= 256, k_local a multiple of 64, n_out a multiple of
+ * 128 * world, n_out / 128 tiles resident at once (n_out <= 18,944 on a B200).
+ * No reference counterpart for the collective: the reference runs on one GPU
+ * (world = 1 is the plain projection). */
+typedef struct vk_oproj vk_oproj;
+vk_status vk_oproj_create(int32_t device, int32_t rank, int32_t world, int32_t max_tokens,
+                          int32_t k_local, int32_t n_out, vk_oproj** out);
+vk_status vk_oproj_export(const vk_oproj* h, void* handle_out);   /* VK_GATHER_HANDLE_BYTES */
+vk_status vk_oproj_import(vk_oproj* h, int32_t peer, const void* handle);
+vk_status vk_oproj_import_local(vk_oproj* h, int32_t peer, const vk_oproj* peer_h);
+vk_status vk_oproj_release_peers(vk_oproj* h);
+vk_status vk_oproj_destroy(vk_oproj* h);
+/* k splits per tile the runs use (CTAs = n_out/128 * splits); -1 for NULL. */
+int32_t   vk_oproj_splits(const vk_oproj* h);
+vk_status vk_oproj_run(vk_oproj* h, const void* x, int32_t ldx, const void* w_t, int32_t ldw,
+                       void* y, int32_t ldy, int32_t tokens, void* stream);
+/* Synchronous: VK_TIMEOUT if a run's wait gave up since the last check. */
+vk_status vk_oproj_check(vk_oproj* h);
+vk_status vk_oproj_pack_weight(const float* w, int32_t ldw, int32_t k_rows, int32_t n, void* w_t,
+                               void* stream);
+
 /* ---- K3: chunked prefill -------------------------------------------------
  * The prefill use of launch_attention (src/transformer.cpp:136-189 with
  * num_tokens = chunk, src/engine.cpp:70-101): query token t of sequence b sits

@@ -64,6 +64,8 @@ def lib():
         L.or_append_fp8.restype = _c_int
         L.or_dequant_fp8.argtypes = [_u8p] + [_c_int] * 5 + [_f32p]
         L.or_rope.restype = None
+        L.or_matmul.argtypes = [_f32p, _f32p, _f32p] + [_c_int] * 4
+        L.or_matmul.restype = None
         _LIB = L
     return _LIB
 
@@ -84,6 +86,8 @@ def ref_lib():
         R.ref_kernels_random_floats.restype = None
         R.ref_cpu_rope.argtypes = [_f32p, _c_int, _c_int, ctypes.c_float, _f32p]
         R.ref_cpu_rope.restype = None
+        R.ref_launch_matmul.argtypes = [ctypes.c_void_p] * 3 + [_c_int] * 3
+        R.ref_launch_matmul.restype = None
         _REF = R
     return _REF
 
@@ -353,3 +357,19 @@ def prefill_fp8(pool_u8, g: Geom, layer, q, block_tables, positions, scale=0.0):
             p = np.exp(s - s.max(axis=1, keepdims=True))
             out[b, :, h] = (p / p.sum(axis=1, keepdims=True)) @ V[h // G]
     return out
+
+
+# ---------------------------------------------------------------- wo projection
+
+def matmul(A, B, nthreads=8):
+    """launch_matmul's contract (cuda/matmul.cu:42-103): fp32 C = A @ B with one
+    in-order fused multiply-add chain per element, as the reference kernel runs."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError("inner dimensions differ")
+    C = np.empty((M, N), np.float32)
+    lib().or_matmul(A.reshape(-1), B.reshape(-1), C.reshape(-1), M, K, N, nthreads)
+    return C

@@ -1,5 +1,6 @@
-// C-linkage handles onto the reference library's own MemoryManager, KVCache and
-// launch_attention (cuda/memory.cu, src/kv_cache.cpp, cuda/attention.cu), so
+// C-linkage handles onto the reference library's own MemoryManager, KVCache,
+// launch_attention and launch_matmul (cuda/memory.cu, src/kv_cache.cpp,
+// cuda/attention.cu, cuda/matmul.cu), so
 // GPU tests can run the reference implementation beside the new library.
 // Test infrastructure only.  Note: the reference's CUDA_CHECK exits the
 // process on a CUDA error.
@@ -39,6 +40,10 @@ size_t ref_kv_memory(void* c) { return static_cast<KVCache*>(c)->memory_usage();
 void ref_launch_attention(const float* Q, const float* K, const float* V, float* O, int b, int h,
                           int s, int d) {
     vulcan::cuda::launch_attention(Q, K, V, O, b, h, s, d);
+}
+
+void ref_launch_matmul(const float* A, const float* B, float* C, int m, int k, int n) {
+    vulcan::cuda::launch_matmul(A, B, C, m, k, n);
 }
 
 }  // extern "C"

@@ -15,6 +15,8 @@
  *                             applied to Q and K_new at src/transformer.cpp:114-128)
  *   - group quantisation      docs/ADRs/003-quantization-format.md:11-18 (symmetric
  *                             per-group fp32 scale; FP8 pages use it with e4m3)
+ *   - launch_matmul           cuda/matmul.cu:42-103            (C = A * B, the wo
+ *                             projection of src/transformer.cpp:191-194)
  *
  * Floating point follows cpu_attention exactly: fp32 accumulation in the same
  * loop order, -FLT_MAX fill, max-subtracted expf, divide by the sum, then the
@@ -501,4 +503,24 @@ void or_e4m3_encode_array(const float* x, uint8_t* out, int64_t n) {
 
 void or_e4m3_decode_array(const uint8_t* c, float* out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = or_e4m3_decode(c[i]);
+}
+
+/* launch_matmul's contract (cuda/matmul.cu:42-103): C[M,N] = A[M,K] * B[K,N],
+ * all row-major fp32.  matmul_kernel gives each output element to one thread
+ * that starts from 0 and adds A[row,k] * B[k,col] for k = 0..K-1 in order (tile
+ * by tile, k inside a tile in order); nvcc compiles `sum += a * b` into one
+ * fused multiply-add, so this loop uses fmaf in the same order and matches the
+ * compiled reference bit for bit. */
+void or_matmul(const float* A, const float* B, float* C, int M, int K, int N, int nthreads) {
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(static)
+#endif
+    for (int row = 0; row < M; ++row) {
+        for (int col = 0; col < N; ++col) {
+            float sum = 0.0f;
+            for (int k = 0; k < K; ++k) sum = fmaf(A[(int64_t)row * K + k], B[(int64_t)k * N + col], sum);
+            C[(int64_t)row * N + col] = sum;
+        }
+    }
 }

@@ -121,3 +121,64 @@ def test_head_sharded_decode_two_gpus(cuda_ok):
             p.kill()
             p.join()
     assert dict(results) == {0: True, 1: True}, dict(results)
+
+
+def _oproj_worker(rank, world, port, results):
+    """Head-sharded output projection: rank r holds the attention output of its
+    heads and its rows of wo; one vk_oproj run per step leaves on rank r its
+    features of x @ wo (a reduce-scatter inside the GEMM launch)."""
+    import sys
+    sys.path.insert(0, ROOT)
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        import torch.distributed as dist
+        import vulcan_b200 as vk
+        import oracle
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        rng = np.random.default_rng(12)
+        tokens, K, N = 48, 2048, 2048
+        x = (rng.standard_normal((tokens, K)) * 0.5).astype(np.float16)
+        w = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)   # wo [K, N]
+        kl, nl = K // world, N // world
+        xr = torch.from_numpy(np.ascontiguousarray(x[:, rank * kl:(rank + 1) * kl])).to(dev)
+        wtr = torch.from_numpy(np.ascontiguousarray(w[rank * kl:(rank + 1) * kl].T)).to(dev)  # [N, kl]
+        op = vk.OutputProjection(rank, world, 64, kl, N, device=dev)
+        op.exchange()
+        outs = [op.run(xr, wtr).clone() for _ in range(3)]
+        torch.cuda.synchronize()
+        op.check()
+        same = all(torch.equal(o, outs[0]) for o in outs[1:])
+        ref = oracle.matmul(x.astype(np.float32), np.ascontiguousarray(w[:, rank * nl:(rank + 1) * nl]).astype(np.float32))
+        got = outs[0].float().cpu().numpy()
+        err = np.abs(got - ref)
+        ok = same and bool((err <= 2e-3 + 1e-2 * np.abs(ref)).all())
+        results[rank] = ok if ok else "same %s max err %g" % (same, err.max())
+        op.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        results[rank] = "exception: " + traceback.format_exc(limit=3)
+
+
+def test_output_projection_reduce_scatter_multi_gpu(cuda_ok):
+    """On every visible GPU (2 to 8): each rank's features of the projection
+    match the oracle's fp32 GEMM of the full x and wo, three runs in a row
+    give the same bits (alternating receive slots)."""
+    n = min(torch.cuda.device_count(), 8)
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _port()
+    procs = [ctx.Process(target=_oproj_worker, args=(r, n, port, results)) for r in range(n)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert dict(results) == {r: True for r in range(n)}, dict(results)

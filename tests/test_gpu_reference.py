@@ -1,7 +1,8 @@
 """GPU tests that run the reference's own implementation (compiled from its
 sources into oracle/_ref) beside the library on identical inputs:
 MemoryManager id sequences and swap results, KVCache::append row placement,
-launch_attention outputs on the reference's six attention cases."""
+launch_attention outputs on the reference's six attention cases, and
+launch_matmul against the oracle's restatement (bit for bit)."""
 import ctypes
 import os
 
@@ -30,6 +31,7 @@ def ref(cuda_ok):
         "ref_kv_destroy": (None, [vp]), "ref_kv_append": (None, [vp, ci, vp, vp, ci, ci]),
         "ref_kv_get": (None, [vp, ci, ctypes.POINTER(vp), ctypes.POINTER(vp)]), "ref_kv_len": (ci, [vp]),
         "ref_kv_memory": (csz, [vp]), "ref_launch_attention": (None, [vp, vp, vp, vp, ci, ci, ci, ci]),
+        "ref_launch_matmul": (None, [vp, vp, vp, ci, ci, ci]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(R, name)
@@ -173,3 +175,19 @@ def test_reference_memory_usage_formula(ref, vk):
     finally:
         ref.ref_kv_destroy(rc)
     assert vk.KVCache(8, 2048, 128, 32).memory_usage() == 2 * 32 * 8 * 2048 * 128 * 2  # fp16 pages
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 512), (7, 300, 130), (64, 1024, 256), (33, 77, 65)])
+def test_oracle_matmul_matches_reference_launch_matmul(ref, m, k, n):
+    """Pins oracle.matmul: the reference's own launch_matmul (cuda/matmul.cu,
+    compiled from its sources, run on the GPU) gives the same fp32 bits."""
+    rng = np.random.default_rng(m + k + n)
+    a = (rng.standard_normal((m, k)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal((k, n)) * 0.02).astype(np.float32)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dc = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    ref.ref_launch_matmul(vp(da.data_ptr()), vp(db.data_ptr()), vp(dc.data_ptr()), m, k, n)
+    torch.cuda.synchronize()
+    got = oracle.matmul(a, b)
+    assert np.array_equal(dc.cpu().numpy().view(np.uint32), got.view(np.uint32)), \
+        "max diff %g" % np.abs(dc.cpu().numpy() - got).max()

@@ -333,3 +333,32 @@ def test_fp8_oracle_prefill_last_row_is_decode():
     pre = oracle.prefill_fp8(pool, g, 0, q, bt, pos)
     dec = oracle.decode_fp8(pool, g, 0, q[:, -1], bt, lens)
     assert np.allclose(pre[:, -1], dec, rtol=1e-12, atol=1e-12)
+
+
+def test_oracle_matmul_contract():
+    """oracle.matmul restates launch_matmul (cuda/matmul.cu:42-103): C = A @ B,
+    fp32, one in-order fused multiply-add chain per element (checked against an
+    explicit fmaf-order loop on a small case and float64 on a larger one)."""
+    from fractions import Fraction
+
+    def fma32(x, y, z):  # x*y + z rounded once to the nearest float32 (ties to even)
+        exact = Fraction(float(x)) * Fraction(float(y)) + Fraction(float(z))
+        c = np.float32(float(exact))
+        best = min((c, np.nextafter(c, np.float32(np.inf)), np.nextafter(c, np.float32(-np.inf))),
+                   key=lambda v: (abs(Fraction(float(v)) - exact), int(v.view(np.uint32)) & 1))
+        return np.float32(best)
+
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((3, 5)).astype(np.float32)
+    b = rng.standard_normal((5, 4)).astype(np.float32)
+    c = oracle.matmul(a, b)
+    for i in range(3):
+        for j in range(4):
+            s = np.float32(0)
+            for k in range(5):
+                s = fma32(a[i, k], b[k, j], s)
+            assert c[i, j] == s
+    a = (rng.standard_normal((17, 700)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal((700, 33)) * 0.02).astype(np.float32)
+    c = oracle.matmul(a, b)
+    assert np.abs(c - a.astype(np.float64) @ b.astype(np.float64)).max() < 1e-5

@@ -70,6 +70,16 @@ SIGNATURES = {
     "vk_gather_export": (c_i32, [vp, vp]),
     "vk_gather_import": (c_i32, [vp, c_i32, vp]),
     "vk_gather_import_local": (c_i32, [vp, c_i32, vp]),
+    "vk_oproj_create": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, vp]),
+    "vk_oproj_export": (c_i32, [vp, vp]),
+    "vk_oproj_import": (c_i32, [vp, c_i32, vp]),
+    "vk_oproj_import_local": (c_i32, [vp, c_i32, vp]),
+    "vk_oproj_release_peers": (c_i32, [vp]),
+    "vk_oproj_destroy": (c_i32, [vp]),
+    "vk_oproj_splits": (c_i32, [vp]),
+    "vk_oproj_run": (c_i32, [vp, vp, c_i32, vp, c_i32, vp, c_i32, c_i32, vp]),
+    "vk_oproj_check": (c_i32, [vp]),
+    "vk_oproj_pack_weight": (c_i32, [vp, c_i32, c_i32, c_i32, vp, vp]),
     "vk_gather_buffer": (vp, [vp, c_i32]),
     "vk_decode_plan_gather_wait": (c_i32, [vp, vp, c_i32, vp]),
     "vk_gather_check": (c_i32, [vp]),

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -78,6 +79,9 @@ struct DeviceGuard {
         if (prev >= 0) cudaSetDevice(prev);
     }
 };
+
+// cuTensorMapEncodeTiled from the driver (NULL when unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn();
 
 // Kernel launchers (defined in the .cu files).
 vk_status launch_append(vk_pool* pool, int layer, const void* k, const void* v, bool f32,

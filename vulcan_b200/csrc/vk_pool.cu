@@ -78,7 +78,7 @@ void Allocator::set_free(int32_t id) {
 
 // ---------------------------------------------------------------- tensor map
 
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -101,7 +101,7 @@ static vk_status make_tmap(vk_pool* p) {
         static_cast<uint64_t>(p->num_pages) * p->cfg.num_layers * p->cfg.num_kv_heads * 2 *
         p->cfg.page_tokens;
     if (rows >= (1ull << 31)) return VK_OK;  // TMA coordinates are int32: kernels refuse
-    auto encode = get_encode_fn();
+    auto encode = tmap_encode_fn();
     if (!encode) return fail(VK_CUDA_ERROR, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(p->cfg.head_dim), rows};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(p->cfg.head_dim) * 2};

@@ -66,6 +66,12 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return pol;
 }
 
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte
 // aligned) from global into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,

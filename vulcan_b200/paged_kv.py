@@ -471,6 +471,100 @@ class Gather:
             pass
 
 
+class OutputProjection:
+    """vk_oproj: the `wo` projection after head-sharded attention fused with its
+    reduce-scatter over output features (see include/vk_paged_kv.h).
+
+    Every rank creates one with the same world, max_tokens, k_local (its heads
+    x head_dim) and n_out; peers are joined like a Gather (``exchange`` over
+    torch.distributed, or ``import_local`` for ranks of this process).  ``run``
+    takes this rank's attention output x [tokens, k_local] fp16 and its rows of
+    wo transposed, w_t [n_out, k_local] fp16, and returns y [tokens,
+    n_out/world] fp16: this rank's features of the sum over ranks."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rank: int, world: int, max_tokens: int, k_local: int, n_out: int, device=None):
+        self._lib = _lib.load()
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                           (device.index if isinstance(device, torch.device) else int(device)))
+        self.device, self.rank, self.world = dev, rank, world
+        self.max_tokens, self.k_local, self.n_out = max_tokens, k_local, n_out
+        h = ctypes.c_void_p()
+        check(self._lib.vk_oproj_create(dev.index, rank, world, max_tokens, k_local, n_out, ctypes.byref(h)),
+              "vk_oproj_create")
+        self.handle = h
+        self._ipc_peers = False
+
+    @property
+    def splits(self) -> int:
+        return self._lib.vk_oproj_splits(self.handle)
+
+    def export(self) -> bytes:
+        buf = ctypes.create_string_buffer(self.HANDLE_BYTES)
+        check(self._lib.vk_oproj_export(self.handle, buf), "vk_oproj_export")
+        return buf.raw
+
+    def import_peer(self, peer: int, handle: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(handle), self.HANDLE_BYTES)
+        check(self._lib.vk_oproj_import(self.handle, peer, buf), "vk_oproj_import")
+        self._ipc_peers = True
+
+    def import_local(self, peer: int, other: "OutputProjection") -> None:
+        check(self._lib.vk_oproj_import_local(self.handle, peer, other.handle), "vk_oproj_import_local")
+
+    def exchange(self, group=None) -> None:
+        import torch.distributed as dist
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.export(), group=group)
+        for r, hd in enumerate(handles):
+            if r != self.rank:
+                self.import_peer(r, hd)
+
+    def run(self, x: torch.Tensor, w_t: torch.Tensor, y: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """x, w_t and y may be row-strided views (unit stride along a row)."""
+        for t, name in ((x, "x"), (w_t, "w_t")) + (((y, "y"),) if y is not None else ()):
+            if t.dtype != torch.float16 or not t.is_cuda or t.dim() != 2 or t.stride(1) != 1:
+                raise ValueError("%s must be a 2-D fp16 CUDA tensor with unit stride along its rows" % name)
+        tokens = x.shape[0]
+        if y is None:
+            y = torch.empty(tokens, self.n_out // self.world, dtype=torch.float16, device=x.device)
+        check(self._lib.vk_oproj_run(self.handle, _ptr(x), x.stride(0), _ptr(w_t), w_t.stride(0), _ptr(y),
+                                     y.stride(0), tokens, _stream(stream)), "vk_oproj_run")
+        return y
+
+    @staticmethod
+    def pack_weight(w: torch.Tensor, stream=None) -> torch.Tensor:
+        """fp32 wo rows [k_rows, n] (the reference's layout) -> fp16 [n, k_rows]."""
+        _need(w, torch.float32, "w")
+        k_rows, n = w.shape
+        wt = torch.empty(n, k_rows, dtype=torch.float16, device=w.device)
+        check(_lib.load().vk_oproj_pack_weight(_ptr(w), w.stride(0), k_rows, n, _ptr(wt), _stream(stream)),
+              "vk_oproj_pack_weight")
+        return wt
+
+    def check(self) -> None:
+        check(self._lib.vk_oproj_check(self.handle), "vk_oproj_check")
+
+    def close(self, group=None) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            if self.world > 1:
+                check(self._lib.vk_oproj_release_peers(self.handle), "vk_oproj_release_peers")
+                if self._ipc_peers:
+                    import torch.distributed as dist
+                    dist.barrier(group=group)
+            self._lib.vk_oproj_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            if getattr(self, "handle", None) is not None and self.handle.value:
+                self._lib.vk_oproj_destroy(self.handle)
+                self.handle = ctypes.c_void_p()
+        except Exception:
+            pass
+
+
 def remap_block_tables(block_tables: torch.Tensor, page_map: torch.Tensor, stream=None) -> None:
     _need(block_tables, torch.int32, "block_tables")
     _need(page_map, torch.int32, "page_map")
