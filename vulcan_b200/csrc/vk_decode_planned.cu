@@ -57,6 +57,9 @@ constexpr int kMinPagesPerWorker = 8;
 constexpr int64_t kUnitEndPages = 6;  // cost of a unit end inside a worker range, in pages (measured best of 0-16)
 constexpr int kLastMergeMax = 8;   // large shares: units of up to this many pieces merge in their last piece
 constexpr int kLastMergeMinPages = 64;  // ... when workers have at least this many pages
+// Merge counters are polled by many warps at once: one 128-byte line each, so
+// the pollers of one unit do not queue behind those of its neighbours.
+constexpr int kCtrStride = 32;
 
 struct PlanParams {
     const int32_t* wb;     // [W+1] first global page of each worker
@@ -68,7 +71,7 @@ struct PlanParams {
     const int32_t* uslot;  // [U]   first partial slot of the unit (-1 if one piece)
     const int32_t* tunits; // [ntasks / S] unit of each merge task group
     const int32_t* zunits; // [Z]   units without pages (zero output)
-    uint32_t* counters;    // [2U] pieces finished, merge tasks finished (reset by the merger / last task)
+    uint32_t* counters;    // [2U lines of kCtrStride] pieces finished, merge tasks finished (reset by the merger / last task)
     float* part_o;         // [slots, G, D]
     float* part_lse;       // [slots, G]
     const __half* q;
@@ -295,7 +298,7 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
         int ok = 1;
         if (lane == 0) {
             const uint64_t t0 = global_ns();
-            while (ld_acquire_gpu(&p.counters[u]) < static_cast<unsigned int>(np)) {
+            while (ld_acquire_gpu(&p.counters[u * kCtrStride]) < static_cast<unsigned int>(np)) {
                 // give up at once if a piece's warp already gave up on a wait
                 if ((*reinterpret_cast<volatile uint32_t*>(p.err) & VK_ERR_TIMEOUT) ||
                     global_ns() - t0 > kGatherWaitNs) {
@@ -316,9 +319,9 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
             else merge_task<D, NT, 16, FMT>(p, u, h0, hs, np, lane);
         }
         __syncwarp();
-        if (lane == 0 && atomicAdd(&p.counters[p.U + u], 1u) == static_cast<unsigned int>(p.S - 1)) {
-            p.counters[u] = 0u;  // every task of the unit has passed its wait
-            p.counters[p.U + u] = 0u;
+        if (lane == 0 && atomicAdd(&p.counters[(p.U + u) * kCtrStride], 1u) == static_cast<unsigned int>(p.S - 1)) {
+            p.counters[u * kCtrStride] = 0u;  // every task of the unit has passed its wait
+            p.counters[(p.U + u) * kCtrStride] = 0u;
         }
     }
 }
@@ -598,11 +601,11 @@ __global__ void __launch_bounds__(kPlanWarps * 32, FMT ? 6 : 1) planned_decode_k
                 }
                 __syncwarp();  // every lane's partial stores precede lane 0's release
                 if (npieces > p.lmm) {
-                    if (lane == 0) atom_add_release_gpu(&p.counters[u], 1u);
+                    if (lane == 0) atom_add_release_gpu(&p.counters[u * kCtrStride], 1u);
                 } else {
                     // few pieces: the last to finish merges the unit at once
                     unsigned int prev = 0;
-                    if (lane == 0) prev = atom_add_acq_rel_gpu(&p.counters[u], 1u);
+                    if (lane == 0) prev = atom_add_acq_rel_gpu(&p.counters[u * kCtrStride], 1u);
                     prev = __shfl_sync(0xffffffffu, prev, 0);
                     if (prev == static_cast<unsigned int>(npieces - 1)) {
                         __syncwarp();  // lane 0's acquire precedes every lane's loads
@@ -611,7 +614,7 @@ __global__ void __launch_bounds__(kPlanWarps * 32, FMT ? 6 : 1) planned_decode_k
                         for (int hg = 0; hg < p.G; hg += HG)
                             merge_task<D, NT, (HG * D / 128 < NT * 8 * D / 128 ? HG * D / 128 : NT * 8 * D / 128), FMT>(
                                 p, u, hg, min(HG, p.G - hg), npieces, lane);
-                        if (lane == 0) p.counters[u] = 0u;
+                        if (lane == 0) p.counters[u * kCtrStride] = 0u;
                     }
                 }
             }
@@ -849,7 +852,7 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     put(zunits, &pl->o_z);
     pl->tables_bytes = t.size() * sizeof(int32_t);
     pl->counters_off = align256(pl->tables_bytes);
-    pl->part_o_off = align256(pl->counters_off + static_cast<size_t>(2 * U) * sizeof(uint32_t));
+    pl->part_o_off = align256(pl->counters_off + static_cast<size_t>(2 * U) * kCtrStride * sizeof(uint32_t));
     pl->part_lse_off = align256(pl->part_o_off + static_cast<size_t>(slots) * G * D * sizeof(float));
     pl->ws_bytes = align256(pl->part_lse_off + static_cast<size_t>(slots) * G * sizeof(float));
     *out_plan = pl;
@@ -875,7 +878,7 @@ vk_status vk_decode_plan_upload(const vk_decode_plan* plan, void* workspace, siz
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(plan tables)");
     if (plan->U > 0) {
         e = cudaMemsetAsync(static_cast<char*>(workspace) + plan->counters_off, 0,
-                            static_cast<size_t>(2 * plan->U) * sizeof(uint32_t), st);
+                            static_cast<size_t>(2 * plan->U) * kCtrStride * sizeof(uint32_t), st);
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(plan counters)");
     }
     return VK_OK;
