@@ -794,9 +794,9 @@ def run_attn_wo(args, wl):
     q = (torch.randn(L, B, hq_l, D, device=dev, generator=gen) * 0.5).half()
     kn = (torch.randn(L, B, hkv_l, D, device=dev, generator=gen) * 0.5).half()
     vn = (torch.randn(L, B, hkv_l, D, device=dev, generator=gen) * 0.5).half()
-    w_t = torch.empty(L, hidden, k_local, device=dev, dtype=torch.float16)  # this rank's rows of wo, transposed
-    for l in range(L):
-        w_t[l].copy_(torch.randn(hidden, k_local, device=dev, generator=gen) * 0.02)
+    # this rank's rows of wo per layer, packed once (as at model load)
+    w_t = [vk.OutputProjection.pack_weight_t16((torch.randn(hidden, k_local, device=dev, generator=gen) * 0.02).half())
+           for _ in range(L)]
     att = torch.empty(L, B, hq_l, D, device=dev, dtype=torch.float16)
     y = torch.empty(L, B, hidden // world, device=dev, dtype=torch.float16)
     op = vk.OutputProjection(rank, world, B, k_local, hidden, device=dev)
@@ -806,19 +806,43 @@ def run_attn_wo(args, wl):
     plan_ws = torch.empty(pool.plan(lens_host, hq_l).workspace.numel() + 4096, dtype=torch.uint8, device=dev)
     keep = {}
 
-    def step(ev=None):
+    def new_plan():
         p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
         p_.set_early_start(True)
         p_.upload()
         keep["plan"] = p_
-        cur = torch.cuda.current_stream(dev)
+
+    def layers():
+        p_ = keep["plan"]
         for l in range(L):
             p_.run(l, q[l], bt_d, out=att[l], k_new=kn[l], v_new=vn[l])
-            if ev is not None:
-                ev[l][0].record(cur)
             op.run(att[l].view(B, k_local), w_t[l], y=y[l])
-            if ev is not None:
-                ev[l][1].record(cur)
+
+    graph = None
+    if not args.eager:
+        # the L-layer step as one CUDA graph (the projection keeps its run
+        # number on the device, so replays are valid)
+        try:
+            new_plan()
+            layers()
+            torch.cuda.synchronize(dev)
+            g_ = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(device=dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.graph(g_, stream=cap):
+                layers()
+            torch.cuda.current_stream(dev).wait_stream(cap)
+            graph = g_
+        except Exception as exc:  # capture refused: launch eagerly
+            print("graph capture failed (%s); eager launches" % exc, file=sys.stderr)
+            graph = None
+
+    def step():
+        new_plan()
+        if graph is not None:
+            graph.replay()
+        else:
+            layers()
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -841,12 +865,16 @@ def run_attn_wo(args, wl):
         barrier()
     ms = t0.elapsed_time(t1) / args.steps
     clocks = clk.summary()
-    # the projection alone: events around each launch (one more step)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    # the projection alone: all layers' projections back to back (each with its
+    # own weights, so every launch streams its 8192 x k_local weights from HBM)
     barrier()
-    step(ev)
+    t0.record()
+    for _ in range(2):
+        for l in range(L):
+            op.run(att[l].view(B, k_local), w_t[l], y=y[l])
+    t1.record()
     barrier()
-    op_ms = statistics.mean(ev[l][0].elapsed_time(ev[l][1]) for l in range(L))
+    op_ms = t0.elapsed_time(t1) / (2 * L)
     op.check()
     pool.check()
     if world > 1:
@@ -872,7 +900,9 @@ def run_attn_wo(args, wl):
                 "vs_baseline": None, "dtype": "f16 (fp32 accumulation, fp32 partial sums)",
                 "data": "synthetic (seeded N(0,0.5^2) K/V/Q, wo ~ N(0, 0.02^2))",
                 "config": workload_config(wl, "fp16", world),
-                "run": {"launch": "eager: per layer vk_decode_run (early start) + vk_oproj_run (cooperative)",
+                "run": {"launch": ("CUDA graph of" if graph is not None else "eager:") +
+                           " per layer vk_decode_run (early start) + vk_oproj_run (cooperative); projection "
+                           "launch time from 2L projections back to back",
                         "oproj_splits": op.splits, "oproj_ctas": (hidden // 128) * op.splits},
                 "per_layer_us": ms * 1e3 / L,
                 "step_hbm_gbs": (ab["total"] + hbm_b) * L / (ms * 1e-3) / 1e9,

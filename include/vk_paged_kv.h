@@ -317,15 +317,20 @@ vk_status vk_decode_plan_gather_wait(const vk_decode_plan* plan, void* workspace
  * attention output of its heads ([tokens, k_local] fp16: the [B, Hq/world, D]
  * decode output), and the same rows of wo; y = sum_r x_r * wo[rows of r].  A
  * run leaves on rank r the output features [r*n_out/world, (r+1)*n_out/world)
- * of y ([tokens, n_out/world] fp16, row stride ldy): a reduce-scatter over
+ * of y ([tokens, n_out/world] fp16, row stride ldy, a multiple of 4, y 8-byte
+ * aligned): a reduce-scatter over
  * features in the same launch as the tcgen05 GEMM, partial tiles stored into
  * their owner's memory over NVLink as they finish (no NCCL call).  fp16 inputs,
  * fp32 accumulation and fp32 partial sums, summed in rank order.
  *
- * Weights: w_t is this rank's rows of wo transposed, [n_out, k_local] fp16 with
- * row stride ldw (an nn.Linear [out, in] weight's column slice).
- * vk_oproj_pack_weight converts the reference's fp32 wo rows ([k_rows, n],
- * row stride ldw) into that layout.
+ * Weights: this rank's rows of wo, packed once (per model load) into the
+ * kernel's layout, vk_oproj_packed_bytes(k_local, n_out) bytes: 16 KiB blocks
+ * of 128 output features x 64 k, each in the 128-byte-swizzled order the
+ * tensor cores read, so every pipeline stage streams one contiguous block.
+ * vk_oproj_pack_weight packs the reference's fp32 wo rows ([k_rows, n], row
+ * stride ldw); vk_oproj_pack_weight_t16 packs fp16 rows of wo transposed
+ * ([n, k_rows], row stride ldw: an nn.Linear [out, in] weight or its column
+ * slice for this rank).
  *
  * Setup mirrors the gather (vk_gather_*): create on every rank with the same
  * world, max_tokens, k_local and n_out; export / import the handles (or
@@ -346,12 +351,16 @@ vk_status vk_oproj_release_peers(vk_oproj* h);
 vk_status vk_oproj_destroy(vk_oproj* h);
 /* k splits per tile the runs use (CTAs = n_out/128 * splits); -1 for NULL. */
 int32_t   vk_oproj_splits(const vk_oproj* h);
-vk_status vk_oproj_run(vk_oproj* h, const void* x, int32_t ldx, const void* w_t, int32_t ldw,
+vk_status vk_oproj_run(vk_oproj* h, const void* x, int32_t ldx, const void* w_packed,
                        void* y, int32_t ldy, int32_t tokens, void* stream);
 /* Synchronous: VK_TIMEOUT if a run's wait gave up since the last check. */
 vk_status vk_oproj_check(vk_oproj* h);
-vk_status vk_oproj_pack_weight(const float* w, int32_t ldw, int32_t k_rows, int32_t n, void* w_t,
+/* Bytes of a packed weight (0 unless k_rows % 64 == 0 and n % 128 == 0). */
+size_t    vk_oproj_packed_bytes(int32_t k_rows, int32_t n);
+vk_status vk_oproj_pack_weight(const float* w, int32_t ldw, int32_t k_rows, int32_t n, void* w_packed,
                                void* stream);
+vk_status vk_oproj_pack_weight_t16(const void* w_t, int32_t ldw, int32_t n, int32_t k_rows,
+                                   void* w_packed, void* stream);
 
 /* ---- K3: chunked prefill -------------------------------------------------
  * The prefill use of launch_attention (src/transformer.cpp:136-189 with

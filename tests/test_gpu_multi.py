@@ -144,8 +144,9 @@ def _oproj_worker(rank, world, port, results):
         w = (rng.standard_normal((K, N)) * 0.02).astype(np.float16)   # wo [K, N]
         kl, nl = K // world, N // world
         xr = torch.from_numpy(np.ascontiguousarray(x[:, rank * kl:(rank + 1) * kl])).to(dev)
-        wtr = torch.from_numpy(np.ascontiguousarray(w[rank * kl:(rank + 1) * kl].T)).to(dev)  # [N, kl]
         op = vk.OutputProjection(rank, world, 64, kl, N, device=dev)
+        # this rank's rows of wo, in the reference's fp32 layout, packed
+        wtr = op.pack_weight(torch.from_numpy(np.ascontiguousarray(w[rank * kl:(rank + 1) * kl]).astype(np.float32)).to(dev))
         op.exchange()
         outs = [op.run(xr, wtr).clone() for _ in range(3)]
         torch.cuda.synchronize()

@@ -35,8 +35,8 @@ def test_oproj_one_rank_matches_oracle(vk, tokens, k, n):
     rng = np.random.default_rng(tokens * 7 + k + n)
     x, w = _inputs(rng, tokens, k, n)
     op = vk.OutputProjection(0, 1, max(tokens, 64), k, n)
-    wt = torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
-    y = op.run(torch.from_numpy(x).cuda(), wt)
+    wp = op.pack_weight(torch.from_numpy(w.astype(np.float32)).cuda())  # the reference's fp32 wo rows
+    y = op.run(torch.from_numpy(x).cuda(), wp)
     torch.cuda.synchronize()
     op.check()
     ref = oracle.matmul(x.astype(np.float32), w.astype(np.float32))
@@ -45,9 +45,9 @@ def test_oproj_one_rank_matches_oracle(vk, tokens, k, n):
 
 
 def test_oproj_strided_inputs_and_output(vk):
-    """x and w_t given as column slices of wider arrays (a rank's heads of the
-    full attention output, its columns of the nn.Linear weight), y written into
-    a wider buffer."""
+    """x given as a column slice of the full attention output (a rank's heads),
+    the weight packed from a column slice of the nn.Linear [out, in] weight,
+    y written into a wider buffer."""
     rng = np.random.default_rng(5)
     tokens, K, k, n = 24, 1024, 256, 512
     xf, wf = _inputs(rng, tokens, K, n)
@@ -56,7 +56,7 @@ def test_oproj_strided_inputs_and_output(vk):
     xd = torch.from_numpy(xf).cuda()
     wtd = torch.from_numpy(np.ascontiguousarray(wf.T)).cuda()  # [n, K]
     ybig = torch.zeros(tokens, n + 64, dtype=torch.float16, device="cuda")
-    op.run(xd[:, r0:r0 + k], wtd[:, r0:r0 + k], y=ybig[:, :n])
+    op.run(xd[:, r0:r0 + k], op.pack_weight_t16(wtd[:, r0:r0 + k]), y=ybig[:, :n])
     torch.cuda.synchronize()
     ref = oracle.matmul(xf[:, r0:r0 + k].astype(np.float32), wf[r0:r0 + k].astype(np.float32))
     assert_close_attn(ybig[:, :n].float().cpu().numpy(), ref, "strided")
@@ -70,7 +70,7 @@ def test_oproj_repeated_runs_bit_identical(vk):
     rng = np.random.default_rng(6)
     x, w = _inputs(rng, 64, 2048, 4096)
     op = vk.OutputProjection(0, 1, 64, 2048, 4096)
-    xd, wtd = torch.from_numpy(x).cuda(), torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
+    xd, wtd = torch.from_numpy(x).cuda(), op.pack_weight_t16(torch.from_numpy(np.ascontiguousarray(w.T)).cuda())
     first = op.run(xd, wtd).clone()
     for _ in range(5):
         assert torch.equal(op.run(xd, wtd), first)
@@ -78,13 +78,28 @@ def test_oproj_repeated_runs_bit_identical(vk):
     op.close()
 
 
-def test_oproj_pack_weight(vk):
+def _packed_reference(w16):
+    """The packed layout restated on the host: 16 KiB blocks [n/128][k/64] of
+    128 rows (features) x 64 k, 16-byte chunk c of row r at c ^ (r % 8)."""
+    k, n = w16.shape
+    out = np.zeros((n // 128, k // 64, 128, 8, 8), np.float16)
+    wt = w16.T.reshape(n // 128, 128, k // 64, 8, 8)  # [tile, r, kb, chunk, e]
+    for r in range(128):
+        for c in range(8):
+            out[:, :, r, c ^ (r & 7), :] = wt[:, r, :, c, :]
+    return out.reshape(-1).view(np.uint8)
+
+
+def test_oproj_pack_weight_layouts(vk):
+    """Both packers produce the same bytes, equal to the layout restated here."""
     rng = np.random.default_rng(7)
-    w = (rng.standard_normal((300, 130)) * 0.02).astype(np.float32)
-    wt = vk.OutputProjection.pack_weight(torch.from_numpy(w).cuda())
+    w = (rng.standard_normal((192, 256)) * 0.02).astype(np.float32)  # [k_rows, n]
+    a = vk.OutputProjection.pack_weight(torch.from_numpy(w).cuda())
+    b = vk.OutputProjection.pack_weight_t16(torch.from_numpy(np.ascontiguousarray(w.T.astype(np.float16))).cuda())
     torch.cuda.synchronize()
-    assert wt.shape == (130, 300)
-    assert np.array_equal(wt.cpu().numpy(), w.T.astype(np.float16))
+    want = _packed_reference(w.astype(np.float16))
+    assert np.array_equal(a.cpu().numpy(), want)
+    assert np.array_equal(b.cpu().numpy(), want)
 
 
 def test_oproj_rejects_bad_arguments(vk):
@@ -96,9 +111,11 @@ def test_oproj_rejects_bad_arguments(vk):
         vk.OutputProjection(0, 1, 300, 128, 256)      # more than 256 tokens
     op = vk.OutputProjection(0, 1, 32, 128, 256)
     x = torch.zeros(33, 128, dtype=torch.float16, device="cuda")
-    wt = torch.zeros(256, 128, dtype=torch.float16, device="cuda")
+    wp = op.pack_weight_t16(torch.zeros(256, 128, dtype=torch.float16, device="cuda"))
     with pytest.raises(vk.VKError):
-        op.run(x, wt)                                 # more tokens than max_tokens
+        op.run(x, wp)                                 # more tokens than max_tokens
+    with pytest.raises(ValueError):
+        op.run(x[:8], wp[:100])                       # not a packed weight of this shape
     op.close()
 
 
@@ -113,7 +130,7 @@ def test_oproj_wait_times_out(vk):
     a, b = vk.OutputProjection(0, 2, 16, 256, 512), vk.OutputProjection(1, 2, 16, 256, 512)
     a.import_local(1, b)
     b.import_local(0, a)
-    xd, wtd = torch.from_numpy(x).cuda(), torch.from_numpy(np.ascontiguousarray(w.T)).cuda()
+    xd, wtd = torch.from_numpy(x).cuda(), a.pack_weight_t16(torch.from_numpy(np.ascontiguousarray(w.T)).cuda())
     torch.cuda.synchronize()
     t0 = time.monotonic()
     a.run(xd, wtd)

@@ -77,9 +77,11 @@ SIGNATURES = {
     "vk_oproj_release_peers": (c_i32, [vp]),
     "vk_oproj_destroy": (c_i32, [vp]),
     "vk_oproj_splits": (c_i32, [vp]),
-    "vk_oproj_run": (c_i32, [vp, vp, c_i32, vp, c_i32, vp, c_i32, c_i32, vp]),
+    "vk_oproj_run": (c_i32, [vp, vp, c_i32, vp, vp, c_i32, c_i32, vp]),
     "vk_oproj_check": (c_i32, [vp]),
+    "vk_oproj_packed_bytes": (c_sz, [c_i32, c_i32]),
     "vk_oproj_pack_weight": (c_i32, [vp, c_i32, c_i32, c_i32, vp, vp]),
+    "vk_oproj_pack_weight_t16": (c_i32, [vp, c_i32, c_i32, c_i32, vp, vp]),
     "vk_gather_buffer": (vp, [vp, c_i32]),
     "vk_decode_plan_gather_wait": (c_i32, [vp, vp, c_i32, vp]),
     "vk_gather_check": (c_i32, [vp]),

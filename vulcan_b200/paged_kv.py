@@ -479,8 +479,10 @@ class OutputProjection:
     x head_dim) and n_out; peers are joined like a Gather (``exchange`` over
     torch.distributed, or ``import_local`` for ranks of this process).  ``run``
     takes this rank's attention output x [tokens, k_local] fp16 and its rows of
-    wo transposed, w_t [n_out, k_local] fp16, and returns y [tokens,
-    n_out/world] fp16: this rank's features of the sum over ranks."""
+    wo packed by ``pack_weight`` (fp32 [k_local, n_out] rows, the reference's
+    layout) or ``pack_weight_t16`` (fp16 [n_out, k_local] rows of wo
+    transposed), and returns y [tokens, n_out/world] fp16: this rank's features
+    of the sum over ranks."""
 
     HANDLE_BYTES = 64
 
@@ -521,27 +523,47 @@ class OutputProjection:
             if r != self.rank:
                 self.import_peer(r, hd)
 
-    def run(self, x: torch.Tensor, w_t: torch.Tensor, y: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-        """x, w_t and y may be row-strided views (unit stride along a row)."""
-        for t, name in ((x, "x"), (w_t, "w_t")) + (((y, "y"),) if y is not None else ()):
+    def run(self, x: torch.Tensor, w_packed: torch.Tensor, y: Optional[torch.Tensor] = None,
+            stream=None) -> torch.Tensor:
+        """x and y may be row-strided views (unit stride along a row)."""
+        for t, name in ((x, "x"),) + (((y, "y"),) if y is not None else ()):
             if t.dtype != torch.float16 or not t.is_cuda or t.dim() != 2 or t.stride(1) != 1:
                 raise ValueError("%s must be a 2-D fp16 CUDA tensor with unit stride along its rows" % name)
+        nbytes = self._lib.vk_oproj_packed_bytes(self.k_local, self.n_out)
+        if not w_packed.is_cuda or w_packed.numel() * w_packed.element_size() != nbytes:
+            raise ValueError("w_packed must be a packed weight of %d bytes (pack_weight / pack_weight_t16)" % nbytes)
         tokens = x.shape[0]
         if y is None:
             y = torch.empty(tokens, self.n_out // self.world, dtype=torch.float16, device=x.device)
-        check(self._lib.vk_oproj_run(self.handle, _ptr(x), x.stride(0), _ptr(w_t), w_t.stride(0), _ptr(y),
-                                     y.stride(0), tokens, _stream(stream)), "vk_oproj_run")
+        check(self._lib.vk_oproj_run(self.handle, _ptr(x), x.stride(0), _ptr(w_packed), _ptr(y), y.stride(0),
+                                     tokens, _stream(stream)), "vk_oproj_run")
         return y
 
     @staticmethod
     def pack_weight(w: torch.Tensor, stream=None) -> torch.Tensor:
-        """fp32 wo rows [k_rows, n] (the reference's layout) -> fp16 [n, k_rows]."""
-        _need(w, torch.float32, "w")
+        """fp32 wo rows [k_rows, n] (the reference's layout, row-strided view
+        allowed) -> packed fp16 weight (uint8 tensor)."""
+        if w.dtype != torch.float32 or not w.is_cuda or w.dim() != 2 or w.stride(1) != 1:
+            raise ValueError("w must be a 2-D fp32 CUDA tensor with unit stride along its rows")
         k_rows, n = w.shape
-        wt = torch.empty(n, k_rows, dtype=torch.float16, device=w.device)
-        check(_lib.load().vk_oproj_pack_weight(_ptr(w), w.stride(0), k_rows, n, _ptr(wt), _stream(stream)),
+        lib = _lib.load()
+        wp = torch.empty(max(1, lib.vk_oproj_packed_bytes(k_rows, n)), dtype=torch.uint8, device=w.device)
+        check(lib.vk_oproj_pack_weight(_ptr(w), w.stride(0), k_rows, n, _ptr(wp), _stream(stream)),
               "vk_oproj_pack_weight")
-        return wt
+        return wp
+
+    @staticmethod
+    def pack_weight_t16(w_t: torch.Tensor, stream=None) -> torch.Tensor:
+        """fp16 rows of wo transposed [n, k_rows] (an nn.Linear [out, in] weight
+        or its column slice) -> packed fp16 weight (uint8 tensor)."""
+        if w_t.dtype != torch.float16 or not w_t.is_cuda or w_t.dim() != 2 or w_t.stride(1) != 1:
+            raise ValueError("w_t must be a 2-D fp16 CUDA tensor with unit stride along its rows")
+        n, k_rows = w_t.shape
+        lib = _lib.load()
+        wp = torch.empty(max(1, lib.vk_oproj_packed_bytes(k_rows, n)), dtype=torch.uint8, device=w_t.device)
+        check(lib.vk_oproj_pack_weight_t16(_ptr(w_t), w_t.stride(0), n, k_rows, _ptr(wp), _stream(stream)),
+              "vk_oproj_pack_weight_t16")
+        return wp
 
     def check(self) -> None:
         check(self._lib.vk_oproj_check(self.handle), "vk_oproj_check")
