@@ -53,6 +53,11 @@ namespace vk {
 
 constexpr int kPlanWarps = 2;      // worker warps per CTA
 constexpr int kPlanStages = 4;     // TMA stages per worker (8 KiB each at D=128)
+// Small per-GPU shares (few pages per worker, fp16 pages, head_dim 128): 3
+// stages per worker and 4 CTAs per SM, i.e. 8 worker warps per SM instead of 6;
+// measured on the 8-GPU share of the 70B layer (10 pages per worker).
+constexpr int kSmallStages = 3;
+constexpr int kSmallSharePages = 16;  // pages per worker below which the small-share kernel runs
 constexpr int kMinPagesPerWorker = 8;
 constexpr int64_t kUnitEndPages = 6;  // cost of a unit end inside a worker range, in pages (measured best of 0-16)
 constexpr int kLastMergeMax = 8;   // large shares: units of up to this many pieces merge in their last piece
@@ -102,9 +107,9 @@ __host__ __device__ constexpr int plan_stage_bytes() {
     return FMT ? fp8_head_bytes(D) : 2 * kPageTokens * D * 2;
 }
 
-template <int D, int FMT>
+template <int D, int FMT, int NS = kPlanStages>
 __host__ __device__ constexpr int plan_smem_bytes() {
-    return kPlanWarps * kPlanStages * plan_stage_bytes<D, FMT>() + kPlanWarps * kPlanStages * 8 + 1024;
+    return kPlanWarps * NS * plan_stage_bytes<D, FMT>() + kPlanWarps * NS * 8 + 1024;
 }
 
 // Programmatic dependent launch: let the next kernel on the stream start
@@ -329,14 +334,13 @@ __device__ __forceinline__ void run_merge_tasks(const PlanParams& p, int w, int 
 // FP8 pools: 6 CTAs (12 worker warps) per SM, measured 9% faster than 4 CTAs
 // on fewer registers (the FP8 page update is bound by per-warp latency, not by
 // bytes in flight).
-template <int D, int NT, int FMT>
-__global__ void __launch_bounds__(kPlanWarps * 32, FMT ? 6 : 1) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
+template <int D, int NT, int FMT, int NS>
+__global__ void __launch_bounds__(kPlanWarps * 32, FMT ? 6 : (NS == kSmallStages ? 4 : 1)) planned_decode_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                          const PlanParams p) {
     constexpr int P = kPageTokens;
     constexpr int SB = plan_stage_bytes<D, FMT>();
     constexpr int NB = D / 64;
     constexpr int KS = D / 16;
-    constexpr int NS = kPlanStages;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -641,17 +645,17 @@ __global__ void plan_gather_wait_kernel(const GatherView g, int slot, const uint
     }
 }
 
-template <int D, int NT, int FMT>
+template <int D, int NT, int FMT, int NS>
 static int plan_occupancy(int device, int* occ_out) {
     static int cache[64] = {};
     if (device < 0 || device >= 64) return -1;
     if (cache[device] == 0) {
-        constexpr int smem = plan_smem_bytes<D, FMT>();
-        if (cudaFuncSetAttribute(planned_decode_kernel<D, NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        constexpr int smem = plan_smem_bytes<D, FMT, NS>();
+        if (cudaFuncSetAttribute(planned_decode_kernel<D, NT, FMT, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return -1;
         int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, planned_decode_kernel<D, NT, FMT>, kPlanWarps * 32, smem) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, planned_decode_kernel<D, NT, FMT, NS>, kPlanWarps * 32, smem) !=
                 cudaSuccess ||
             occ <= 0)
             return -1;
@@ -661,12 +665,15 @@ static int plan_occupancy(int device, int* occ_out) {
     return 0;
 }
 
-static int occupancy_for(int D, int NT, int fmt, int device, int* occ) {
+static int occupancy_for(int D, int NT, int fmt, int ns, int device, int* occ) {
+    constexpr int S = kPlanStages, s3 = kSmallStages;
     if (fmt == VK_KV_FP8)  // FP8 pools: head_dim 128 only
-        return NT == 1 ? plan_occupancy<128, 1, 1>(device, occ) : plan_occupancy<128, 2, 1>(device, occ);
-    if (D == 128) return NT == 1 ? plan_occupancy<128, 1, 0>(device, occ) : plan_occupancy<128, 2, 0>(device, occ);
-    if (D == 64) return NT == 1 ? plan_occupancy<64, 1, 0>(device, occ) : plan_occupancy<64, 2, 0>(device, occ);
-    return NT == 1 ? plan_occupancy<256, 1, 0>(device, occ) : plan_occupancy<256, 2, 0>(device, occ);
+        return NT == 1 ? plan_occupancy<128, 1, 1, S>(device, occ) : plan_occupancy<128, 2, 1, S>(device, occ);
+    if (D == 128 && ns == s3)
+        return NT == 1 ? plan_occupancy<128, 1, 0, s3>(device, occ) : plan_occupancy<128, 2, 0, s3>(device, occ);
+    if (D == 128) return NT == 1 ? plan_occupancy<128, 1, 0, S>(device, occ) : plan_occupancy<128, 2, 0, S>(device, occ);
+    if (D == 64) return NT == 1 ? plan_occupancy<64, 1, 0, S>(device, occ) : plan_occupancy<64, 2, 0, S>(device, occ);
+    return NT == 1 ? plan_occupancy<256, 1, 0, S>(device, occ) : plan_occupancy<256, 2, 0, S>(device, occ);
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -674,7 +681,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 }  // namespace vk
 
 struct vk_decode_plan {
-    int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1, fmt = VK_KV_FP16;
+    int device = 0, B = 0, Hq = 0, Hkv = 0, G = 0, D = 0, NT = 1, fmt = VK_KV_FP16, ns = vk::kPlanStages;
     int W = 0, U = 0, Z = 0, slots = 0, grid = 0, max_unit_pages = 0, total_pages = 0;
     mutable std::vector<int32_t> tables;
     size_t o_wb = 0, o_wfu = 0, o_uoff = 0, o_ulen = 0, o_ufw = 0, o_unp = 0, o_uslot = 0, o_tu = 0, o_z = 0;
@@ -739,17 +746,25 @@ vk_status vk_decode_plan_create(const vk_pool* pool, const int32_t* seq_lens_hos
     pl->total_pages = static_cast<int>(T);
     pl->Z = static_cast<int>(zunits.size());
     int occ = 1;
-    {
+    int64_t cap = 0, W = 0;
+    auto size_workers = [&]() -> bool {
         DeviceGuard g(pool->device);
-        if (occupancy_for(D, pl->NT, pl->fmt, pool->device, &occ) != 0) {
-            delete pl;
-            return fail(VK_CUDA_ERROR, "occupancy query for the planned decode kernel failed");
-        }
+        if (occupancy_for(D, pl->NT, pl->fmt, pl->ns, pool->device, &occ) != 0) return false;
+        cap = static_cast<int64_t>(pool->num_sms) * occ * kPlanWarps;
+        if (pool->plan_workers > 0) cap = std::min<int64_t>(cap, pool->plan_workers);
+        W = T > 0 ? std::min<int64_t>(cap, (T + kMinPagesPerWorker - 1) / kMinPagesPerWorker) : 0;
+        W = std::max<int64_t>(W, T > 0 ? 1 : 0);
+        return true;
+    };
+    bool sized = size_workers();
+    if (sized && pl->fmt == VK_KV_FP16 && D == 128 && W > 0 && T / W < kSmallSharePages) {
+        pl->ns = kSmallStages;  // small share: more, shallower workers
+        sized = size_workers();
     }
-    int64_t cap = static_cast<int64_t>(pool->num_sms) * occ * kPlanWarps;
-    if (pool->plan_workers > 0) cap = std::min<int64_t>(cap, pool->plan_workers);
-    int64_t W = T > 0 ? std::min<int64_t>(cap, (T + kMinPagesPerWorker - 1) / kMinPagesPerWorker) : 0;
-    W = std::max<int64_t>(W, T > 0 ? 1 : 0);
+    if (!sized) {
+        delete pl;
+        return fail(VK_CUDA_ERROR, "occupancy query for the planned decode kernel failed");
+    }
     pl->W = static_cast<int>(W);
     // with long worker ranges a unit's few pieces end at different times: the
     // last merges at once; with short ranges (small per-GPU shares) all pieces
@@ -1027,7 +1042,7 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
     int occ = 0;
-    if (occupancy_for(D, plan->NT, plan->fmt, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
+    if (occupancy_for(D, plan->NT, plan->fmt, plan->ns, pool->device, &occ) != 0) return fail(VK_CUDA_ERROR, "kernel attribute setup failed");
     const dim3 grid(plan->grid), block(kPlanWarps * 32);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1039,15 +1054,17 @@ vk_status vk_decode_run(vk_pool* pool, const vk_decode_plan* plan, int32_t layer
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t le = cudaSuccess;
-#define VK_LAUNCH(DD, NN, FF)                                                               \
-    do {                                                                                    \
-        cfg.dynamicSmemBytes = plan_smem_bytes<DD, FF>();                                   \
-        le = cudaLaunchKernelEx(&cfg, planned_decode_kernel<DD, NN, FF>, pool->tmap, p);    \
+#define VK_LAUNCH(DD, NN, FF, SS)                                                               \
+    do {                                                                                        \
+        cfg.dynamicSmemBytes = plan_smem_bytes<DD, FF, SS>();                                   \
+        le = cudaLaunchKernelEx(&cfg, planned_decode_kernel<DD, NN, FF, SS>, pool->tmap, p);    \
     } while (0)
-    if (plan->fmt == VK_KV_FP8) { if (plan->NT == 1) VK_LAUNCH(128, 1, 1); else VK_LAUNCH(128, 2, 1); }
-    else if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1, 0); else VK_LAUNCH(128, 2, 0); }
-    else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1, 0); else VK_LAUNCH(64, 2, 0); }
-    else { if (plan->NT == 1) VK_LAUNCH(256, 1, 0); else VK_LAUNCH(256, 2, 0); }
+    constexpr int S4 = kPlanStages, S3 = kSmallStages;
+    if (plan->fmt == VK_KV_FP8) { if (plan->NT == 1) VK_LAUNCH(128, 1, 1, S4); else VK_LAUNCH(128, 2, 1, S4); }
+    else if (D == 128 && plan->ns == S3) { if (plan->NT == 1) VK_LAUNCH(128, 1, 0, S3); else VK_LAUNCH(128, 2, 0, S3); }
+    else if (D == 128) { if (plan->NT == 1) VK_LAUNCH(128, 1, 0, S4); else VK_LAUNCH(128, 2, 0, S4); }
+    else if (D == 64) { if (plan->NT == 1) VK_LAUNCH(64, 1, 0, S4); else VK_LAUNCH(64, 2, 0, S4); }
+    else { if (plan->NT == 1) VK_LAUNCH(256, 1, 0, S4); else VK_LAUNCH(256, 2, 0, S4); }
 #undef VK_LAUNCH
     if (le != cudaSuccess) return cuda_fail(le, "planned_decode_kernel launch");
     cudaError_t e = cudaGetLastError();
