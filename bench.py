@@ -534,6 +534,26 @@ def main():
             dec_src = "step time / layers (events unavailable)"
     clocks = clk.summary()
 
+    # --- each decode launch timed alone: one more step launched eagerly, no
+    # early start, CUDA events around every launch (median over the layers)
+    iso_ms = None
+    if args.path == "planned":
+        p_iso = pool.plan(lens_host, hq_l, workspace=plan_ws)
+        p_iso.upload()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+        barrier()
+        for l in range(L):
+            evs[l][0].record(compute)
+            p_iso.run(l, q[l], bt_d, out=out[l], k_new=kn3[l], v_new=vn3[l])
+            evs[l][1].record(compute)
+        barrier()
+        iso_ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+        if world > 1:
+            t = torch.tensor([iso_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            iso_ms = float(t.item())
+        pool.check()
+
     # --- DRAM traffic per launch from the committed ncu capture (70B, 1 GPU, planned)
     traffic, traffic_src = None, None
     if (args.config == "70b" and world == 1 and args.path == "planned" and not args.layers and not args.batch
@@ -598,6 +618,10 @@ def main():
                          "kernel": ("vk_decode_run (planned: append + decode + merge in one launch)"
                                     if args.path == "planned" else "vk_decode (split grid + merge)"),
                          "peak_source": peak_kind, "launch_ms": dec_avg_ms, "launch_timing": dec_src,
+                         "launch_ms_alone": iso_ms,
+                         "frac_alone": (ab_local["decode"] / (iso_ms * 1e-3) / 1e9 / peak) if iso_ms else None,
+                         "alone_timing": "median over the layers of one more step launched eagerly without early "
+                                         "start, CUDA events around each launch" if iso_ms else None,
                          "algorithmic_bytes_per_launch": ab_local["decode"]},
             "cpu_baseline": cpu,
             "e2e": e2e,
