@@ -97,7 +97,8 @@ vk_status vk_pool_create_in(const vk_pool_cfg* cfg, void* device_mem, size_t byt
  * K and 16 V scales.  head_dim 128 and page_tokens 16 only.  FP8 pools take
  * vk_append, vk_append_f32 (quantising), the planned decode (vk_decode_plan_*,
  * vk_decode_run, fused append included), vk_decode and vk_decode_static,
- * vk_prefill (its mma.sync kernel; prefill path 2 is refused), allocation,
+ * vk_prefill (the tcgen05 kernel with FP8-to-fp16 converter warps, or the
+ * mma.sync kernel with prefill path 1), allocation,
  * copy and swap. */
 #define VK_KV_FP16 0
 #define VK_KV_FP8  1
@@ -385,9 +386,9 @@ vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, void* out,
 vk_status vk_set_rope(vk_pool* pool, float theta_base);
 
 /* Selects the prefill kernel for the pool: 0 = automatic (the tcgen05/TMEM
- * kernel for head_dim 128, the mma.sync kernel otherwise), 1 = the mma.sync
- * kernel, 2 = the tcgen05 kernel (VK_UNSUPPORTED from vk_prefill for other
- * head dims). */
+ * kernel for head_dim 128, fp16 or FP8 pages; the mma.sync kernel otherwise),
+ * 1 = the mma.sync kernel, 2 = the tcgen05 kernel (VK_UNSUPPORTED from
+ * vk_prefill for other head dims). */
 vk_status vk_set_prefill_path(vk_pool* pool, int32_t path);
 
 /* ---- K4: page copy (fork / compaction; no reference counterpart) -----------

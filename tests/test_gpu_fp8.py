@@ -181,13 +181,16 @@ def test_fp8_split_decode(vk, pps):
     assert_close_attn(out.float().cpu().numpy(), ref, "FP8 split decode, pages per split %d" % pps)
 
 
+@pytest.mark.parametrize("path", [1, 2])
 @pytest.mark.parametrize("rope", [False, True])
-def test_fp8_prefill(vk, rope):
-    """Chunked prefill over FP8 pages (the mma.sync kernel): the chunk's rows are
-    appended (quantised) first, then each chunk row attends the cached prefix
-    and the chunk up to itself."""
-    rng = np.random.default_rng(89 + rope)
-    Hq, Hkv, D, L, layer, T = 8, 2, 128, 2, 1, 130
+def test_fp8_prefill(vk, rope, path):
+    """Chunked prefill over FP8 pages, on the mma.sync kernel (path 1) and on the
+    tcgen05 kernel with converter warps (path 2, the default): the chunk's rows
+    are appended (quantised) first, then each chunk row attends the cached
+    prefix and the chunk up to itself.  Several key tiles, a partial last page,
+    two row tiles per CTA and a ragged last one."""
+    rng = np.random.default_rng(89 + rope + 10 * path)
+    Hq, Hkv, D, L, layer, T = 8, 2, 128, 2, 1, 300
     pos = np.array([0, 900, 37], np.int32)
     g = oracle.Geom(L, Hkv, D, 16, 0)
     bt, g.num_pages = random_layout(rng, pos + T)
@@ -204,6 +207,7 @@ def test_fp8_prefill(vk, rope):
                        for b in range(B)])
     assert oracle.append_fp8(host, g, layer, kk, vc, bt, pos) == 0
     q = rows(rng, B, T, Hq, D)
+    pool.set_prefill_path(path)
     out = pool.prefill(layer, dev_f16(q), dev_i32(bt), dev_i32(pos))
     torch.cuda.synchronize()
     assert pool.check() == 0
@@ -214,10 +218,29 @@ def test_fp8_prefill(vk, rope):
     else:
         assert_bytes(pool, host, "FP8 chunk append")
     ref = oracle.prefill_fp8(host, g, layer, q, bt, pos)
-    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 prefill%s" % (" with RoPE" if rope else ""))
-    pool.set_prefill_path(2)
-    with pytest.raises(vk.VKError):  # the tcgen05 kernel reads fp16 pages only
-        pool.prefill(layer, dev_f16(q), dev_i32(bt), dev_i32(pos))
+    assert_close_attn(out.float().cpu().numpy(), ref, "FP8 prefill path %d%s" % (path, " with RoPE" if rope else ""))
+
+
+def test_fp8_prefill_paths_agree_on_stale_pages(vk):
+    """The FP8 tcgen05 prefill against the mma.sync one on a pool whose unwritten
+    slots hold random bytes (NaN codes included): keys past the written length
+    must not reach the output on either path."""
+    rng = np.random.default_rng(97)
+    Hq, Hkv, D, L, layer, T = 16, 2, 128, 1, 0, 200
+    pos = np.array([5, 250], np.int32)
+    g = oracle.Geom(L, Hkv, D, 16, 0)
+    bt, g.num_pages = random_layout(rng, pos + T + 40)
+    pool, host = fp8_pool(vk, g, rng)
+    fill_history(vk, pool, host, g, rng, layer, bt, pos + 1)
+    pool.append(layer, dev_f16(rows(rng, 2, T, Hkv, D)), dev_f16(rows(rng, 2, T, Hkv, D)), dev_i32(bt), dev_i32(pos))
+    q = dev_f16(rows(rng, 2, T, Hq, D))
+    outs = []
+    for path in (1, 2):
+        pool.set_prefill_path(path)
+        outs.append(pool.prefill(layer, q, dev_i32(bt), dev_i32(pos)).float().cpu().numpy())
+    torch.cuda.synchronize()
+    assert pool.check() == 0
+    assert_close_attn(outs[1], outs[0], "FP8 prefill tcgen05 vs mma.sync")
 
 
 def test_fp8_copy_and_swap(vk):

@@ -426,9 +426,10 @@ extern "C" vk_status vk_prefill(vk_pool* pool, int32_t layer, const void* q, voi
     p.scale_log2 = sc * 1.4426950408889634f;
     DeviceGuard g(pool->device);
     cudaStream_t st = as_stream(stream);
-    if (fp8) {  // FP8 pages (head_dim 128): the mma.sync kernel; the tcgen05 one reads fp16 tiles
-        if (pool->prefill_path == 2) return fail(VK_UNSUPPORTED, "the tcgen05 prefill reads fp16 pages only");
-        return launch_prefill_t<128, 1>(pool, p, batch, st);
+    if (fp8) {  // FP8 pages (head_dim 128): the tcgen05 kernel with converter warps; path 1: mma.sync
+        if (pool->prefill_path == 1) return launch_prefill_t<128, 1>(pool, p, batch, st);
+        return prefill_tc(pool, layer, q, out, block_tables, bt_stride, positions, batch, tokens, num_q_heads, scale,
+                          st);
     }
     const bool tc = D == 128 && pool->prefill_path != 1;
     if (pool->prefill_path == 2 && !tc) return fail(VK_UNSUPPORTED, "the tcgen05 prefill supports head_dim 128");

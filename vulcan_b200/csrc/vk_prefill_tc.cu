@@ -30,6 +30,15 @@
 //  * V stages start zeroed, and V rows of keys at or beyond the written length
 //    in the last key tile are zeroed before that tile's PV, so stale bytes
 //    cannot reach O.  All waits are bounded.
+//  * FP8 pages (FMT 1, vk_fp8.cuh): warp 8 bulk-copies the tile's page blocks
+//    (e4m3 codes + fp32 row scales, 4,224 bytes each) into a staging buffer,
+//    and warps 10-11 dequantise them (code x scale as fp16 pairs; for K the
+//    scale is split into two fp16 parts so it adds no rounding of its own)
+//    into the same swizzled K ring and into a V^T ring (rows of head
+//    dimension, keys contiguous: the FP8 block stores V element-major, so the
+//    conversion writes 16-byte chunks, and PV reads V as a K-major operand).
+//    Keys at or beyond the written length are written as zeros.
+#include "vk_fp8.cuh"
 #include "vk_internal.h"
 #include "vk_ptx.cuh"
 #include "vk_rope.cuh"
@@ -39,7 +48,8 @@ namespace vk {
 
 constexpr int kTcRows = 128;                  // rows of one tile; a CTA has two
 constexpr int kTcKeys = 128;
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 320;               // fp16 pages
+constexpr int kTcThreads8 = 384;              // FP8 pages: two more warps convert
 constexpr int kTcD = 128;
 // shared memory map (bytes from a 1024-aligned base)
 constexpr int kTcQ = 0;                       // [2 tiles][2 halves][128 rows][128 B]
@@ -47,6 +57,11 @@ constexpr int kTcK = 65536;                   // 2 stages x 32 KiB
 constexpr int kTcV = kTcK + 2 * 32768;        // 2 stages x 32 KiB
 constexpr int kTcBar = kTcV + 2 * 32768;      // mbarriers + TMEM address
 constexpr int kTcSmem = kTcBar + 256 + 1024;
+// FP8 pages: a staging buffer for one key tile's page blocks after the V ring
+constexpr int kTcStage8 = kTcBar;                                  // 8 x 4,224 bytes
+constexpr int kTcBar8 = kTcStage8 + (kTcKeys / kPageTokens) * fp8_head_bytes(kTcD);
+constexpr int kTcSmem8 = kTcBar8 + 256 + 1024;
+static_assert(kTcSmem8 <= 232448, "FP8 prefill shared memory");
 constexpr uint32_t kTcCols = 512;
 
 struct TcParams {
@@ -58,6 +73,9 @@ struct TcParams {
     int bt_stride, T, Hq, Hkv, G, layer, num_pages, q_tiles;
     float scale_log2;
     const float* rope_freq;  // non-null: q rotated (RoPE) at its position
+    // FP8 pages: block of (layer, page, head) at pool_base + layer_off + page * seg_bytes + head * head_bytes
+    const char* pool_base;
+    uint64_t layer_off, seg_bytes, head_bytes;
 };
 
 // 3-input max (one instruction on sm_100)
@@ -80,13 +98,15 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, uint32_
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, err));
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap16,
+template <int FMT>
+__global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap16,
                                                                   const TcParams p) {
     constexpr int P = kPageTokens;
+    constexpr int NTHR = FMT ? kTcThreads8 : kTcThreads;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcBar);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (FMT ? kTcBar8 : kTcBar));
     // barrier slots
     uint64_t* k_full = bars + 0;   // [2]
     uint64_t* k_empty = bars + 2;  // [2]
@@ -97,6 +117,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     uint64_t* o_full = bars + 12;  // [tile]   PV of the tile done
     uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (count 256)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* stg_full = bars + 17;   // FP8 [2 halves]: the half-tile's page blocks are in its staging half
+    uint64_t* stg_empty = bars + 19;  // FP8 [2 halves]: the converters are done with that half
 
     const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
     const int h = blockIdx.y, b = blockIdx.z;
@@ -126,10 +148,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
             mbar_init(smem_u32(&o_full[t]), 1);
         }
         mbar_init(smem_u32(q_full), 256);
+        if (FMT) {
+            for (int hf = 0; hf < 2; ++hf) {
+                mbar_init(smem_u32(&stg_full[hf]), 1);
+                mbar_init(smem_u32(&stg_empty[hf]), 1);
+            }
+        }
         mbar_fence_init();
     }
     // zero both V stages: rows a last tile does not load keep finite values
-    for (int i = threadIdx.x; i < 2 * 32768 / 16; i += kTcThreads)
+    for (int i = threadIdx.x; i < 2 * 32768 / 16; i += NTHR)
         asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(sbase + kTcV + i * 16), "r"(0u) : "memory");
     fence_async_smem();
     if (warp == 9) {
@@ -141,7 +169,211 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 8) {
+    if (FMT && warp == 8) {
+        // ------------------------------------------------------------ FP8 page blocks -> staging
+        // Two staging halves of 4 pages: the next half-tile loads while the
+        // converters work on the other half.
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            const int32_t* btrow = p.bt + static_cast<int64_t>(b) * p.bt_stride;
+            constexpr int HB = fp8_head_bytes(kTcD);
+            constexpr int PH = kTcKeys / P / 2;  // pages per half
+            bool ok = true;
+            for (int j = 0; j < ntiles && ok; ++j) {
+                const int npg = min(kTcKeys / P, (kv_len - j * kTcKeys + P - 1) / P);
+                for (int hf = 0; hf < 2; ++hf) {
+                    if (j >= 1 && !mbar_wait(smem_u32(&stg_empty[hf]), (j - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const int n_here = max(0, min(PH, npg - hf * PH));
+                    const uint32_t bar = smem_u32(&stg_full[hf]);
+                    mbar_expect_tx(bar, n_here * HB);  // 0 bytes: the phase completes at once
+                    for (int i = 0; i < n_here; ++i) {
+                        int pg = btrow[j * (kTcKeys / P) + hf * PH + i];
+                        if (pg < 0 || pg >= p.num_pages) {
+                            atomicOr(p.err, VK_ERR_PAGE_ID);
+                            pg = 0;
+                        }
+                        bulk_load(sbase + kTcStage8 + (hf * PH + i) * HB,
+                                  p.pool_base + p.layer_off + static_cast<uint64_t>(pg) * p.seg_bytes +
+                                      static_cast<uint64_t>(hkv) * p.head_bytes,
+                                  HB, bar, pol);
+                    }
+                }
+            }
+        }
+    } else if (FMT && warp >= 10) {
+        // ------------------------------------------------------------ FP8 -> fp16 converters (64 threads)
+        const int ct = threadIdx.x - 320;
+        constexpr int HB = fp8_head_bytes(kTcD);
+        constexpr int PH = kTcKeys / P / 2;
+        volatile int* okp = reinterpret_cast<volatile int*>(tmem_slot) + 1;  // broadcast slot
+        bool alive = true;
+        // K of a staging half: chunk (page, token, 16 elements) -> key row, two
+        // 16-byte fp16 chunks; code x scale as fp16 pairs with the scale split
+        // into s_hi + s_lo (both fp16): t = code * s_hi, then t + code * s_lo,
+        // so the row scale carries no fp16 rounding of its own.  Four chunks
+        // per round, their loads issued first.
+        auto convert_k = [&](int hf, int st, int key_end) {
+#pragma unroll 1
+            for (int i0 = 0; i0 < PH * P * 8 / 64; i0 += 4) {
+                uint4 codes[4];
+                float s1[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int q = ct + 64 * (i0 + u);
+                    const int pg = hf * PH + (q >> 7), t = (q >> 3) & 15, c = q & 7;
+                    const uint32_t src = sbase + kTcStage8 + pg * HB;
+                    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(codes[u].x), "=r"(codes[u].y), "=r"(codes[u].z), "=r"(codes[u].w)
+                                 : "r"(src + fp8_k_off(t, 16 * c, kTcD)));
+                    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(s1[u]) : "r"(src + fp8_scale_off(0, t, kTcD)));
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int q = ct + 64 * (i0 + u);
+                    const int pg = hf * PH + (q >> 7), t = (q >> 3) & 15, c = q & 7, key = pg * P + t;
+                    const __half shi = __float2half_rn(s1[u]);
+                    const __half slo = __float2half_rn(s1[u] - __half2float(shi));
+                    const __half2 hi2 = __half2half2(shi), lo2 = __half2half2(slo);
+                    const uint32_t w[4] = {codes[u].x, codes[u].y, codes[u].z, codes[u].w};
+                    uint32_t o[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        uint32_t a, b2;
+                        e4m3x4_to_h2x2(w[k], a, b2);
+                        const __half2 ca = *reinterpret_cast<const __half2*>(&a);
+                        const __half2 cb = *reinterpret_cast<const __half2*>(&b2);
+                        const __half2 ra = __hfma2(ca, lo2, __hmul2(ca, hi2));
+                        const __half2 rb = __hfma2(cb, lo2, __hmul2(cb, hi2));
+                        o[2 * k] = *reinterpret_cast<const uint32_t*>(&ra);
+                        o[2 * k + 1] = *reinterpret_cast<const uint32_t*>(&rb);
+                    }
+                    if (key >= key_end) {  // past the written length: zeros (the bytes may be anything)
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) o[k] = 0u;
+                    }
+                    const int hb = c >> 2, cc = (c & 3) * 2;
+                    const uint32_t row = sbase + kTcK + st * 32768 + hb * 16384 + key * 128;
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + ((cc ^ (key & 7)) << 4)),
+                                 "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                                 : "memory");
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + (((cc + 1) ^ (key & 7)) << 4)),
+                                 "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7])
+                                 : "memory");
+                }
+            }
+        };
+        // V of a staging half: per page, this thread's rows d = ct and ct + 64 of
+        // V^T (keys pg*16 .. pg*16+15).  The block holds token t at position
+        // fp8_v_pos(t): two byte permutes per 8 codes put the tokens in order,
+        // then codes -> fp16 (exact) times the tokens' scales as fp16 pairs.
+        auto convert_v = [&](int hf, int st, int key_end) {
+#pragma unroll 1
+            for (int pi = 0; pi < PH; ++pi) {
+                const int pg = hf * PH + pi;
+                const int valid = key_end - pg * P;
+                const uint32_t src = sbase + kTcStage8 + pg * HB;
+                uint32_t o[2][8];
+                if (valid > 0) {
+                    uint4 raw[2];
+#pragma unroll
+                    for (int dd = 0; dd < 2; ++dd)
+                        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                     : "=r"(raw[dd].x), "=r"(raw[dd].y), "=r"(raw[dd].z), "=r"(raw[dd].w)
+                                     : "r"(src + fp8_v_off(0, ct + 64 * dd, kTcD)));
+                    float sv[16];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(sv[4 * k]), "=f"(sv[4 * k + 1]), "=f"(sv[4 * k + 2]), "=f"(sv[4 * k + 3])
+                                     : "r"(src + fp8_scale_off(1, 4 * k, kTcD)));
+                    __half2 sp[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)  // keys past the written length: scale 0 (and cleared below)
+                        sp[k] = __floats2half2_rn(2 * k < valid ? sv[2 * k] : 0.f, 2 * k + 1 < valid ? sv[2 * k + 1] : 0.f);
+#pragma unroll
+                    for (int dd = 0; dd < 2; ++dd) {
+                        // positions 0..15 hold tokens 0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15
+                        uint32_t nat[4];
+                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[0]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 0 1 2 3
+                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[1]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 4 5 6 7
+                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[2]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 8 9 10 11
+                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[3]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 12 .. 15
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            uint32_t a, b2;
+                            e4m3x4_to_h2x2(nat[k], a, b2);
+                            const __half2 ra = __hmul2(*reinterpret_cast<const __half2*>(&a), sp[2 * k]);
+                            const __half2 rb = __hmul2(*reinterpret_cast<const __half2*>(&b2), sp[2 * k + 1]);
+                            o[dd][2 * k] = *reinterpret_cast<const uint32_t*>(&ra);
+                            o[dd][2 * k + 1] = *reinterpret_cast<const uint32_t*>(&rb);
+                        }
+                        if (valid < P) {  // a NaN code times scale 0 stays NaN: clear those keys
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                if (2 * k >= valid) o[dd][k] &= 0xffff0000u;
+                                if (2 * k + 1 >= valid) o[dd][k] &= 0x0000ffffu;
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int dd = 0; dd < 2; ++dd)
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) o[dd][k] = 0u;
+                }
+                const int hb = pg >> 2, cc = (pg & 3) * 2;
+#pragma unroll
+                for (int dd = 0; dd < 2; ++dd) {
+                    const int d = ct + 64 * dd;
+                    const uint32_t row = sbase + kTcV + st * 32768 + hb * 16384 + d * 128;
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + ((cc ^ (d & 7)) << 4)),
+                                 "r"(o[dd][0]), "r"(o[dd][1]), "r"(o[dd][2]), "r"(o[dd][3])
+                                 : "memory");
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row + (((cc + 1) ^ (d & 7)) << 4)),
+                                 "r"(o[dd][4]), "r"(o[dd][5]), "r"(o[dd][6]), "r"(o[dd][7])
+                                 : "memory");
+                }
+            }
+        };
+        // one converter thread waits, the 64 meet at named barrier 2
+        auto sync_on = [&](uint32_t bar1, uint32_t par1, uint32_t bar2, uint32_t par2, bool second) -> bool {
+            if (ct == 0) {
+                bool ok = mbar_wait(bar1, par1, p.err);
+                if (ok && second) ok = mbar_wait(bar2, par2, p.err);
+                *okp = ok ? 1 : 0;
+            }
+            asm volatile("bar.sync 2, 64;" ::: "memory");
+            return *okp != 0;
+        };
+        // per key tile: K of half 0, K of half 1 (k_full), V of half 0 (staging
+        // half 0 free), V of half 1 (staging half 1 free, v_full): S can start
+        // on a tile whose V is still being converted
+        for (int j = 0; j < ntiles && alive; ++j) {
+            const int st = j & 1;
+            const int key_end = kv_len - j * kTcKeys;  // keys of this tile below the written length
+            const uint32_t ph = j & 1, pe = ((j >> 1) - 1) & 1;
+            if (!sync_on(smem_u32(&stg_full[0]), ph, smem_u32(&k_empty[st]), pe, j >= 2)) break;
+            convert_k(0, st, key_end);
+            if (!sync_on(smem_u32(&stg_full[1]), ph, 0, 0, false)) break;
+            convert_k(1, st, key_end);
+            fence_async_smem();  // the generic-proxy stores precede the tensor core's reads
+            asm volatile("bar.sync 2, 64;" ::: "memory");
+            if (ct == 0) mbar_arrive(smem_u32(&k_full[st]));
+            if (j >= 2 && !sync_on(smem_u32(&v_empty[st]), pe, 0, 0, false)) break;
+            for (int hf = 0; hf < 2; ++hf) {
+                convert_v(hf, st, key_end);
+                fence_async_smem();
+                asm volatile("bar.sync 2, 64;" ::: "memory");
+                if (ct == 0) {
+                    mbar_arrive(smem_u32(&stg_empty[hf]));
+                    if (hf == 1) mbar_arrive(smem_u32(&v_full[st]));
+                }
+            }
+        }
+    } else if (warp == 8) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             prefetch_tmap(&tmap16);
@@ -182,7 +414,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t id_s = idesc_f16_128x128(0), id_pv = idesc_f16_128x128(1);
+            // fp16 pages: V stage [key][d] (B MN-major); FP8 pages: V^T [d][key] (B K-major)
+            const uint32_t id_s = idesc_f16_128x128(0), id_pv = idesc_f16_128x128(FMT ? 0u : 1u);
             bool ok = mbar_wait(smem_u32(q_full), 0, p.err);
             tc_fence_after();
             const int nt[2] = {ntA, ntB};
@@ -193,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
             // warps, and every issue slot it spends delays the tensor pipe.
             const uint64_t dq0 = umma_desc_sw128(sbase + kTcQ, 16, 1024);
             const uint64_t dk0 = umma_desc_sw128(sbase + kTcK, 16, 1024);
-            const uint64_t dv0 = umma_desc_sw128(sbase + kTcV, 16384, 1024);
+            const uint64_t dv0 = FMT ? umma_desc_sw128(sbase + kTcV, 16, 1024) : umma_desc_sw128(sbase + kTcV, 16384, 1024);
             auto issue_s = [&](int t, int j) {
                 const int st = j & 1;
                 if (j > k_waited) {
@@ -227,8 +460,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                 const uint32_t dpo = tmem + 256 + t * 128, dpa = tmem + t * 128;
                 umma_ts(dpo, dpa, dv, id_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-                for (int ks = 1; ks < kTcKeys / 16; ++ks)
-                    umma_ts(dpo, dpa + ks * 8, dv + static_cast<uint64_t>(ks * (2048 >> 4)), id_pv, 1u);
+                for (int ks = 1; ks < kTcKeys / 16; ++ks) {
+                    // next 16 keys: fp16 V advances 16 rows (2 KiB); FP8's V^T 32 bytes
+                    // along its 128-byte rows, then to the second 64-key half
+                    const uint64_t adv = FMT ? static_cast<uint64_t>(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4)
+                                             : static_cast<uint64_t>(ks * (2048 >> 4));
+                    umma_ts(dpo, dpa + ks * 8, dv + adv, id_pv, 1u);
+                }
                 umma_commit(smem_u32(&o_full[t]));
                 if (t == 1 || j >= ntB) umma_commit(smem_u32(&v_empty[st]));
             };
@@ -347,7 +585,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
                 }
             }
             tmem_wait_st();
-            if (j == ntiles - 1 && key0 + kTcKeys > kv_len) {
+            if (!FMT && j == ntiles - 1 && key0 + kTcKeys > kv_len) {
                 // the CTA's last key tile: zero V rows of keys at or beyond the
                 // written length (both tiles may do it; same zeros)
                 if (!wait_warp(smem_u32(&v_full[j & 1]), (j >> 1) & 1, p.err)) { alive = false; break; }
@@ -397,15 +635,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const __grid_
 }
 
 vk_status launch_prefill_tc(vk_pool* pool, const TcParams& p, int B, cudaStream_t st) {
-    static uint64_t attr_set = 0;
+    static uint64_t attr_set[2] = {0, 0};
+    const int fmt = pool->kv_format == VK_KV_FP8 ? 1 : 0;
     const uint64_t bit = 1ull << (pool->device & 63);
-    if (!(attr_set & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (!(attr_set[fmt] & bit)) {
+        cudaError_t e = fmt ? cudaFuncSetAttribute(prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem8)
+                            : cudaFuncSetAttribute(prefill_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
-        attr_set |= bit;
+        attr_set[fmt] |= bit;
     }
     dim3 grid(p.q_tiles, p.Hq, B);
-    prefill_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(pool->tmap16, p);
+    if (fmt) prefill_tc_kernel<1><<<grid, kTcThreads8, kTcSmem8, st>>>(pool->tmap16, p);
+    else prefill_tc_kernel<0><<<grid, kTcThreads, kTcSmem, st>>>(pool->tmap16, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "prefill_tc_kernel launch");
 }
@@ -429,6 +670,10 @@ vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const i
     const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(kTcD));
     p.scale_log2 = sc * 1.4426950408889634f;
     p.rope_freq = pool->rope_freq;
+    p.pool_base = pool->base;
+    p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
+    p.seg_bytes = pool->seg_bytes;
+    p.head_bytes = pool->head_bytes;
     return launch_prefill_tc(pool, p, B, st);
 }
 
