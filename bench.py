@@ -1043,7 +1043,7 @@ def run_prefill(args, wl):
                 "dtype": "f16" if args.kv == "fp16" else "e4m3 K/V pages (fp32 scale per row), f16 MMA, f32 accumulation",
                 "data": "synthetic (seeded N(0,0.5^2) fp16)",
                 "config": {"workload": wl["desc"], "kv_format": args.kv,
-                           "kernel": ("mma.sync FP8-page kernel" if args.kv == "fp8" else
+                           "kernel": ("tcgen05 kernel with FP8-to-fp16 converter warps" if args.kv == "fp8" else
                                       "tcgen05 kernel" if wl["D"] == 128 else "mma.sync kernel"),
                            "launch": "CUDA graph of the %d-layer step" % L,
                            "shard": "sequence x%d" % world if world > 1 else "none"},

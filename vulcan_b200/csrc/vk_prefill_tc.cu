@@ -30,9 +30,10 @@
 //  * V stages start zeroed, and V rows of keys at or beyond the written length
 //    in the last key tile are zeroed before that tile's PV, so stale bytes
 //    cannot reach O.  All waits are bounded.
-//  * FP8 pages (FMT 1, vk_fp8.cuh): warp 8 bulk-copies the tile's page blocks
-//    (e4m3 codes + fp32 row scales, 4,224 bytes each) into a staging buffer,
-//    and warps 10-11 dequantise them (code x scale as fp16 pairs; for K the
+//  * FP8 pages (FMT 1, vk_fp8.cuh): warp 8 bulk-copies each key tile's e4m3
+//    codes and fp32 row scales into a staging buffer, K and V apart (the next
+//    tile's K loads while this tile's V is converted), and warps 10-11
+//    dequantise them (code x scale as fp16 pairs; for K the
 //    scale is split into two fp16 parts so it adds no rounding of its own)
 //    into the same swizzled K ring and into a V^T ring (rows of head
 //    dimension, keys contiguous: the FP8 block stores V element-major, so the
@@ -57,9 +58,15 @@ constexpr int kTcK = 65536;                   // 2 stages x 32 KiB
 constexpr int kTcV = kTcK + 2 * 32768;        // 2 stages x 32 KiB
 constexpr int kTcBar = kTcV + 2 * 32768;      // mbarriers + TMEM address
 constexpr int kTcSmem = kTcBar + 256 + 1024;
-// FP8 pages: a staging buffer for one key tile's page blocks after the V ring
-constexpr int kTcStage8 = kTcBar;                                  // 8 x 4,224 bytes
-constexpr int kTcBar8 = kTcStage8 + (kTcKeys / kPageTokens) * fp8_head_bytes(kTcD);
+// FP8 pages: staging for one key tile after the V ring, K and V apart: each
+// half holds 8 pages' codes (2 KiB each) then their 16 row scales (64 bytes)
+constexpr int kTcStage8 = kTcBar;
+constexpr int kStgCodes = kPageTokens * kTcD;                      // 2,048
+constexpr int kStgScales = (kTcKeys / kPageTokens) * kStgCodes;    // 16,384
+constexpr int kStgHalf = kStgScales + (kTcKeys / kPageTokens) * 64;
+constexpr int kStgPageBytes = kStgCodes + 64;                      // bytes per page and half
+constexpr int kTcBar8 = kTcStage8 + 2 * kStgHalf;
+static_assert(2 * kStgHalf == (kTcKeys / kPageTokens) * 4224, "FP8 staging holds one tile of page blocks");
 constexpr int kTcSmem8 = kTcBar8 + 256 + 1024;
 static_assert(kTcSmem8 <= 232448, "FP8 prefill shared memory");
 constexpr uint32_t kTcCols = 512;
@@ -117,8 +124,8 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     uint64_t* o_full = bars + 12;  // [tile]   PV of the tile done
     uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (count 256)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-    uint64_t* stg_full = bars + 17;   // FP8 [2 halves]: the half-tile's page blocks are in its staging half
-    uint64_t* stg_empty = bars + 19;  // FP8 [2 halves]: the converters are done with that half
+    uint64_t* stg_full = bars + 17;   // FP8 [K, V]: the tile's K (V) codes and scales are staged
+    uint64_t* stg_empty = bars + 19;  // FP8 [K, V]: the converters are done with them
 
     const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x);  // heavy tiles first
     const int h = blockIdx.y, b = blockIdx.z;
@@ -171,34 +178,37 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
 
     if (FMT && warp == 8) {
         // ------------------------------------------------------------ FP8 page blocks -> staging
-        // Two staging halves of 4 pages: the next half-tile loads while the
-        // converters work on the other half.
+        // K and V are staged apart (each page's codes and its scales are two
+        // bulk copies): the next tile's K loads while this tile's V is being
+        // converted, and its V while its K is.
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
             const int32_t* btrow = p.bt + static_cast<int64_t>(b) * p.bt_stride;
-            constexpr int HB = fp8_head_bytes(kTcD);
-            constexpr int PH = kTcKeys / P / 2;  // pages per half
             bool ok = true;
             for (int j = 0; j < ntiles && ok; ++j) {
                 const int npg = min(kTcKeys / P, (kv_len - j * kTcKeys + P - 1) / P);
-                for (int hf = 0; hf < 2; ++hf) {
-                    if (j >= 1 && !mbar_wait(smem_u32(&stg_empty[hf]), (j - 1) & 1, p.err)) {
+                int pages[kTcKeys / P];
+                for (int i = 0; i < npg; ++i) {
+                    int pg = btrow[j * (kTcKeys / P) + i];
+                    if (pg < 0 || pg >= p.num_pages) {
+                        atomicOr(p.err, VK_ERR_PAGE_ID);
+                        pg = 0;
+                    }
+                    pages[i] = pg;
+                }
+                for (int kv = 0; kv < 2; ++kv) {
+                    if (j >= 1 && !mbar_wait(smem_u32(&stg_empty[kv]), (j - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
-                    const int n_here = max(0, min(PH, npg - hf * PH));
-                    const uint32_t bar = smem_u32(&stg_full[hf]);
-                    mbar_expect_tx(bar, n_here * HB);  // 0 bytes: the phase completes at once
-                    for (int i = 0; i < n_here; ++i) {
-                        int pg = btrow[j * (kTcKeys / P) + hf * PH + i];
-                        if (pg < 0 || pg >= p.num_pages) {
-                            atomicOr(p.err, VK_ERR_PAGE_ID);
-                            pg = 0;
-                        }
-                        bulk_load(sbase + kTcStage8 + (hf * PH + i) * HB,
-                                  p.pool_base + p.layer_off + static_cast<uint64_t>(pg) * p.seg_bytes +
-                                      static_cast<uint64_t>(hkv) * p.head_bytes,
-                                  HB, bar, pol);
+                    const uint32_t bar = smem_u32(&stg_full[kv]);
+                    mbar_expect_tx(bar, npg * kStgPageBytes);
+                    const uint32_t dst = sbase + kTcStage8 + kv * kStgHalf;
+                    for (int i = 0; i < npg; ++i) {
+                        const char* blk = p.pool_base + p.layer_off + static_cast<uint64_t>(pages[i]) * p.seg_bytes +
+                                          static_cast<uint64_t>(hkv) * p.head_bytes;
+                        bulk_load(dst + i * kStgCodes, blk + kv * kStgCodes, kStgCodes, bar, pol);
+                        bulk_load(dst + kStgScales + i * 64, blk + fp8_scale_off(kv, 0, kTcD), 64, bar, pol);
                     }
                 }
             }
@@ -206,34 +216,31 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     } else if (FMT && warp >= 10) {
         // ------------------------------------------------------------ FP8 -> fp16 converters (64 threads)
         const int ct = threadIdx.x - 320;
-        constexpr int HB = fp8_head_bytes(kTcD);
-        constexpr int PH = kTcKeys / P / 2;
         volatile int* okp = reinterpret_cast<volatile int*>(tmem_slot) + 1;  // broadcast slot
-        bool alive = true;
-        // K of a staging half: chunk (page, token, 16 elements) -> key row, two
-        // 16-byte fp16 chunks; code x scale as fp16 pairs with the scale split
-        // into s_hi + s_lo (both fp16): t = code * s_hi, then t + code * s_lo,
-        // so the row scale carries no fp16 rounding of its own.  Four chunks
-        // per round, their loads issued first.
-        auto convert_k = [&](int hf, int st, int key_end) {
+        const uint32_t kstg = sbase + kTcStage8, vstg = sbase + kTcStage8 + kStgHalf;
+        // K: chunk (page, token, 16 elements) -> key row, two 16-byte fp16
+        // chunks; code x scale as fp16 pairs with the scale split into s_hi +
+        // s_lo (both fp16): t = code * s_hi, then t + code * s_lo, so the row
+        // scale carries no fp16 rounding of its own.  Four chunks per round,
+        // their loads issued first.
+        auto convert_k = [&](int st, int key_end) {
 #pragma unroll 1
-            for (int i0 = 0; i0 < PH * P * 8 / 64; i0 += 4) {
+            for (int i0 = 0; i0 < kTcKeys * 8 / 64; i0 += 4) {
                 uint4 codes[4];
                 float s1[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int q = ct + 64 * (i0 + u);
-                    const int pg = hf * PH + (q >> 7), t = (q >> 3) & 15, c = q & 7;
-                    const uint32_t src = sbase + kTcStage8 + pg * HB;
+                    const int pg = q >> 7, t = (q >> 3) & 15, c = q & 7;
                     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                                  : "=r"(codes[u].x), "=r"(codes[u].y), "=r"(codes[u].z), "=r"(codes[u].w)
-                                 : "r"(src + fp8_k_off(t, 16 * c, kTcD)));
-                    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(s1[u]) : "r"(src + fp8_scale_off(0, t, kTcD)));
+                                 : "r"(kstg + pg * kStgCodes + fp8_k_off(t, 16 * c, kTcD)));
+                    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(s1[u]) : "r"(kstg + kStgScales + pg * 64 + t * 4));
                 }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int q = ct + 64 * (i0 + u);
-                    const int pg = hf * PH + (q >> 7), t = (q >> 3) & 15, c = q & 7, key = pg * P + t;
+                    const int pg = q >> 7, t = (q >> 3) & 15, c = q & 7, key = pg * P + t;
                     const __half shi = __float2half_rn(s1[u]);
                     const __half slo = __float2half_rn(s1[u] - __half2float(shi));
                     const __half2 hi2 = __half2half2(shi), lo2 = __half2half2(slo);
@@ -265,16 +272,14 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 }
             }
         };
-        // V of a staging half: per page, this thread's rows d = ct and ct + 64 of
-        // V^T (keys pg*16 .. pg*16+15).  The block holds token t at position
-        // fp8_v_pos(t): two byte permutes per 8 codes put the tokens in order,
-        // then codes -> fp16 (exact) times the tokens' scales as fp16 pairs.
-        auto convert_v = [&](int hf, int st, int key_end) {
+        // V: per page, this thread's rows d = ct and ct + 64 of V^T (keys
+        // pg*16 .. pg*16+15).  The block holds token t at position fp8_v_pos(t):
+        // byte permutes put the tokens in order, then codes -> fp16 (exact)
+        // times the tokens' scales as fp16 pairs.
+        auto convert_v = [&](int st, int key_end) {
 #pragma unroll 1
-            for (int pi = 0; pi < PH; ++pi) {
-                const int pg = hf * PH + pi;
+            for (int pg = 0; pg < kTcKeys / P; ++pg) {
                 const int valid = key_end - pg * P;
-                const uint32_t src = sbase + kTcStage8 + pg * HB;
                 uint32_t o[2][8];
                 if (valid > 0) {
                     uint4 raw[2];
@@ -282,13 +287,13 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                     for (int dd = 0; dd < 2; ++dd)
                         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                                      : "=r"(raw[dd].x), "=r"(raw[dd].y), "=r"(raw[dd].z), "=r"(raw[dd].w)
-                                     : "r"(src + fp8_v_off(0, ct + 64 * dd, kTcD)));
+                                     : "r"(vstg + pg * kStgCodes + (ct + 64 * dd) * P));
                     float sv[16];
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
                         asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                                      : "=f"(sv[4 * k]), "=f"(sv[4 * k + 1]), "=f"(sv[4 * k + 2]), "=f"(sv[4 * k + 3])
-                                     : "r"(src + fp8_scale_off(1, 4 * k, kTcD)));
+                                     : "r"(vstg + kStgScales + pg * 64 + 16 * k));
                     __half2 sp[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k)  // keys past the written length: scale 0 (and cleared below)
@@ -297,10 +302,10 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                     for (int dd = 0; dd < 2; ++dd) {
                         // positions 0..15 hold tokens 0,1,8,9,2,3,10,11,4,5,12,13,6,7,14,15
                         uint32_t nat[4];
-                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[0]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 0 1 2 3
-                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[1]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 4 5 6 7
-                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[2]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 8 9 10 11
-                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[3]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 12 .. 15
+                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[0]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 0..3
+                        asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(nat[1]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 4..7
+                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[2]) : "r"(raw[dd].x), "r"(raw[dd].y));  // 8..11
+                        asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(nat[3]) : "r"(raw[dd].z), "r"(raw[dd].w));  // 12..15
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             uint32_t a, b2;
@@ -338,7 +343,7 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 }
             }
         };
-        // one converter thread waits, the 64 meet at named barrier 2
+        // one converter thread waits (bounded), the 64 meet at named barrier 2
         auto sync_on = [&](uint32_t bar1, uint32_t par1, uint32_t bar2, uint32_t par2, bool second) -> bool {
             if (ct == 0) {
                 bool ok = mbar_wait(bar1, par1, p.err);
@@ -348,29 +353,28 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
             asm volatile("bar.sync 2, 64;" ::: "memory");
             return *okp != 0;
         };
-        // per key tile: K of half 0, K of half 1 (k_full), V of half 0 (staging
-        // half 0 free), V of half 1 (staging half 1 free, v_full): S can start
-        // on a tile whose V is still being converted
-        for (int j = 0; j < ntiles && alive; ++j) {
+        // per key tile: K (k_full; the next tile's K starts loading), then V
+        // (v_full; the next tile's V starts loading): S can start on a tile
+        // whose V is still being converted
+        for (int j = 0; j < ntiles; ++j) {
             const int st = j & 1;
             const int key_end = kv_len - j * kTcKeys;  // keys of this tile below the written length
             const uint32_t ph = j & 1, pe = ((j >> 1) - 1) & 1;
             if (!sync_on(smem_u32(&stg_full[0]), ph, smem_u32(&k_empty[st]), pe, j >= 2)) break;
-            convert_k(0, st, key_end);
-            if (!sync_on(smem_u32(&stg_full[1]), ph, 0, 0, false)) break;
-            convert_k(1, st, key_end);
+            convert_k(st, key_end);
             fence_async_smem();  // the generic-proxy stores precede the tensor core's reads
             asm volatile("bar.sync 2, 64;" ::: "memory");
-            if (ct == 0) mbar_arrive(smem_u32(&k_full[st]));
-            if (j >= 2 && !sync_on(smem_u32(&v_empty[st]), pe, 0, 0, false)) break;
-            for (int hf = 0; hf < 2; ++hf) {
-                convert_v(hf, st, key_end);
-                fence_async_smem();
-                asm volatile("bar.sync 2, 64;" ::: "memory");
-                if (ct == 0) {
-                    mbar_arrive(smem_u32(&stg_empty[hf]));
-                    if (hf == 1) mbar_arrive(smem_u32(&v_full[st]));
-                }
+            if (ct == 0) {
+                mbar_arrive(smem_u32(&stg_empty[0]));
+                mbar_arrive(smem_u32(&k_full[st]));
+            }
+            if (!sync_on(smem_u32(&stg_full[1]), ph, smem_u32(&v_empty[st]), pe, j >= 2)) break;
+            convert_v(st, key_end);
+            fence_async_smem();
+            asm volatile("bar.sync 2, 64;" ::: "memory");
+            if (ct == 0) {
+                mbar_arrive(smem_u32(&stg_empty[1]));
+                mbar_arrive(smem_u32(&v_full[st]));
             }
         }
     } else if (warp == 8) {
