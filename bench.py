@@ -1088,6 +1088,8 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     h2d = torch.cuda.Stream(device=dev)
     d2h = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
+    from vulcan_b200.shard import GatherSchedule
+    sched = GatherSchedule(L, slots=2 * L)  # the receive buffer holds 2L slots
     h2d_bytes = (hq.numel() + hk.numel() + hv.numel()) * 2
     d2h_bytes = hout_layers.numel() * 2 + (hout.numel() * 2 if gathered_host else 0)
     plan_keep = {}
@@ -1098,12 +1100,12 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             if gat is not None:
                 # alternate steps write alternate halves of the 2L slots, so a
                 # slot is rewritten only after every rank's copies of it are done
-                p_.set_gather(gat, slot_base=parity * L, wait_prev=args.gather == "p2p-wait")
+                p_.set_gather(gat, slot_base=sched.slot_base(parity + 1), wait_prev=args.gather == "p2p-wait")
             p_.upload()
             plan_keep["plan"] = p_
 
     def layers(parity=0):
-        base = parity * L
+        base = sched.slot_base(parity + 1)
         cur = torch.cuda.current_stream(dev)
         plan = plan_keep.get("plan")
         h2d.wait_stream(cur)

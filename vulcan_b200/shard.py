@@ -76,3 +76,55 @@ def seq_shard(lengths: Sequence[int], world: int) -> List[np.ndarray]:
         owner[i] = r
         loads[r] += int(lengths[i])
     return [np.nonzero(owner == r)[0] for r in range(world)]
+
+
+class GatherSchedule:
+    """Host side of the step protocol of the fused output gather (vk_gather_*
+    bound to a decode plan): which receive slot each layer's run writes, which
+    slot each run raises this rank's flags for, what the end-of-step wait
+    covers, and the flag value (the step epoch) of a step.  The decode library
+    applies the same rules on the device; callers use this to pick each
+    step's ``slot_base`` and to know when a slot may be read or rewritten.
+
+    * Step ``s`` (1-based epoch ``s``) with ``L`` layers: run ``l`` writes slot
+      ``(slot_base + l) % slots``; run ``l > 0`` raises this rank's flag of run
+      ``l - 1``'s slot to the epoch (its stores are complete: the previous grid
+      on the stream has finished); the end-of-step wait raises the last slot's
+      flag and waits until every rank's flag of that slot carries the epoch.
+      Since every rank raises its flags in layer order, that wait covers the
+      whole step.
+    * With ``2 * L`` slots, alternate steps use alternate halves
+      (``slot_base`` 0, L, 0, ...), so a slot written in step ``s`` is rewritten
+      in step ``s + 2``, which no rank begins before every rank has raised its
+      end-of-step flag of step ``s + 1``: a rank's readers of step ``s``'s slots
+      have until it ends step ``s + 1`` (its end-of-step wait) to finish.
+    """
+
+    def __init__(self, layers: int, slots: int = 0):
+        if layers < 1:
+            raise ValueError("layers must be >= 1")
+        self.layers = layers
+        self.slots = slots or 2 * layers
+        if self.slots < layers:
+            raise ValueError("fewer slots than layers")
+        self.epoch = 0  # steps begun
+
+    def begin_step(self) -> int:
+        """Starts the next step; returns its slot_base."""
+        self.epoch += 1
+        return self.slot_base(self.epoch)
+
+    def slot_base(self, epoch: int) -> int:
+        if self.slots >= 2 * self.layers:
+            return ((epoch - 1) % 2) * self.layers
+        return 0
+
+    def slot(self, slot_base: int, layer: int) -> int:
+        return (slot_base + layer) % self.slots
+
+    def raised_by_run(self, slot_base: int, layer: int):
+        """Slot whose flag run ``layer`` raises, or None (layer 0)."""
+        return self.slot(slot_base, layer - 1) if layer > 0 else None
+
+    def slots_of_step(self, slot_base: int) -> List[int]:
+        return [self.slot(slot_base, l) for l in range(self.layers)]
