@@ -21,8 +21,9 @@
 //  * warp 8 lane 0 streams K and V pages with 2-D TMA boxes of 16 rows x 128 B
 //    (128-byte swizzle) into separate 2-stage rings.
 //  * warps 0-3 (tile A) and 4-7 (tile B): one thread per query row (its TMEM
-//    lane).  Per key tile: row max over the S row read from TMEM (masked on the
-//    causal diagonal), P = 2^(s*scale - m) packed to fp16 into TMEM, and O
+//    lane).  Per key tile: the S row read from TMEM once into registers, its
+//    max (masked on the causal diagonal), P = 2^(s*scale - m) packed to fp16
+//    into TMEM, and O
 //    rescaled in TMEM only when the row max grows by more than 2^8 (P stays
 //    <= 2^8; exact after the final divide).  The scale is folded into one FMA
 //    per element, the max (3-input) and sum run as four independent chains,
@@ -92,13 +93,14 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
     return r;
 }
 
-// Causal mask of 64 scores of a row: key k0 + i is hidden when k0 + i > lim.
-__device__ __forceinline__ void mask_row(float (&v)[2][32], int k0, int lim) {
+// Causal mask of a row's scores: key 32c + i is hidden when 32c + i > lim.
+template <int NC>
+__device__ __forceinline__ void mask_row(float (&v)[NC][32], int lim) {
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2)
+    for (int c = 0; c < NC; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            if (k0 + h2 * 32 + i > lim) v[h2][i] = -INFINITY;
+            if (c * 32 + i > lim) v[c][i] = -INFINITY;
 }
 
 __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, uint32_t* err) {
@@ -468,14 +470,13 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 tc_fence_after();
                 const uint64_t dv = dv0 + static_cast<uint64_t>(st * (32768 >> 4));
                 const uint32_t dpo = tmem + 256 + t * 128, dpa = tmem + t * 128;
-                umma_ts(dpo, dpa, dv, id_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-                for (int ks = 1; ks < kTcKeys / 16; ++ks) {
+                for (int ks = 0; ks < kTcKeys / 16; ++ks) {
                     // next 16 keys: fp16 V advances 16 rows (2 KiB); FP8's V^T 32 bytes
                     // along its 128-byte rows, then to the second 64-key half
                     const uint64_t adv = FMT ? static_cast<uint64_t>(((ks >> 2) * 16384 + (ks & 3) * 32) >> 4)
                                              : static_cast<uint64_t>(ks * (2048 >> 4));
-                    umma_ts(dpo, dpa + ks * 8, dv + adv, id_pv, 1u);
+                    umma_ts(dpo, dpa + ks * 8, dv + adv, id_pv, (j > 0 || ks > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&o_full[t]));
                 if (t == 1 || j >= ntB) umma_commit(smem_u32(&v_empty[st]));
@@ -506,9 +507,15 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
         {
             const uint4* src = reinterpret_cast<const uint4*>(
                 p.q + ((static_cast<int64_t>(b) * p.T + (valid_row ? qrow : 0)) * p.Hq + h) * kTcD);
+            // all 16 loads first: a shared store (asm with a memory clobber)
+            // between them would serialise 16 round trips to HBM (~13k cycles
+            // of the CTA's start, measured)
+            uint4 qv[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) qv[c] = valid_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
-                uint4 v = valid_row ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                uint4 v = qv[c];
                 if (p.rope_freq != nullptr) v = rope_uint4(v, c * 8, qpos, p.rope_freq);
                 const uint32_t addr =
                     sbase + kTcQ + t * 32768 + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
@@ -529,26 +536,24 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
             // keys past the tile's first row need the causal mask
             const bool need_mask = key0 + kTcKeys - 1 > pos0 + q0 + t * kTcRows;
             const int lim = qpos - key0;  // key c is visible iff c <= lim
-            // pass 1: row max of the raw scores (scale > 0 commutes with max);
-            // masked keys read as -inf, so their P below is 2^-inf = 0
+            // the whole S row in registers (one TMEM pass); row max of the raw
+            // scores (scale > 0 commutes with max); masked keys read as -inf,
+            // so their P below is 2^-inf = 0
+            float v[kTcKeys / 32][32];
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 32; ++c) tmem_ld32(lane_base + s_col + c * 32, v[c]);
+            tmem_wait_ld();
+            if (need_mask) mask_row(v, lim);
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c2 = 0; c2 < kTcKeys / 64; ++c2) {
-                float v[2][32];
-                tmem_ld32(lane_base + s_col + c2 * 64, v[0]);
-                tmem_ld32(lane_base + s_col + c2 * 64 + 32, v[1]);
-                tmem_wait_ld();
-                if (need_mask) mask_row(v, c2 * 64, lim);
+            for (int c = 0; c < kTcKeys / 32; ++c)
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        mx4[0] = max3f(mx4[0], v[h2][i], v[h2][i + 1]);
-                        mx4[1] = max3f(mx4[1], v[h2][i + 2], v[h2][i + 3]);
-                        mx4[2] = max3f(mx4[2], v[h2][i + 4], v[h2][i + 5]);
-                        mx4[3] = max3f(mx4[3], v[h2][i + 6], v[h2][i + 7]);
-                    }
-            }
+                for (int i = 0; i < 32; i += 8) {
+                    mx4[0] = max3f(mx4[0], v[c][i], v[c][i + 1]);
+                    mx4[1] = max3f(mx4[1], v[c][i + 2], v[c][i + 3]);
+                    mx4[2] = max3f(mx4[2], v[c][i + 4], v[c][i + 5]);
+                    mx4[3] = max3f(mx4[3], v[c][i + 6], v[c][i + 7]);
+                }
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sc;
             float alpha = 1.f;
             if (mx > m_ref + 8.f || m_ref == -INFINITY) {  // lazy rescale
@@ -556,33 +561,9 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 alpha = ex2(m_ref - m_new);
                 m_ref = m_new;
             }
-            // pass 2: P = 2^(s*sc - m_ref), packed to fp16 over the first 64
-            // columns of S (column 16c+i holds keys 32c+2i, 32c+2i+1)
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
-#pragma unroll
-            for (int c2 = 0; c2 < kTcKeys / 64; ++c2) {
-                float v[2][32];
-                tmem_ld32(lane_base + s_col + c2 * 64, v[0]);
-                tmem_ld32(lane_base + s_col + c2 * 64 + 32, v[1]);
-                tmem_wait_ld();
-                if (need_mask) mask_row(v, c2 * 64, lim);
-#pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float a0 = ex2(fmaf(v[h2][i], sc, mneg));
-                        const float a1 = ex2(fmaf(v[h2][i + 1], sc, mneg));
-                        sum4[(i >> 1) & 3] += a0 + a1;
-                        pk[i >> 1] = pack_half2(a0, a1);
-                    }
-                    tmem_st16(lane_base + s_col + (2 * c2 + h2) * 16, pk);
-                }
-            }
-            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             // tcgen05.ld/st are warp-collective: rescale O if any row of the warp
-            // needs it (PV of the previous tile completed before this S was written)
+            // needs it (PV of the previous tile completed before this S was written), before any
+            // PV of this tile starts
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
                 for (int c = 0; c < kTcD / 32; ++c) {
@@ -594,10 +575,10 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                     tmem_st32(lane_base + o_col + c * 32, v);
                 }
             }
-            tmem_wait_st();
             if (!FMT && j == ntiles - 1 && key0 + kTcKeys > kv_len) {
                 // the CTA's last key tile: zero V rows of keys at or beyond the
-                // written length (both tiles may do it; same zeros)
+                // written length before any PV of it (both tiles may do it; same
+                // zeros)
                 if (!wait_warp(smem_u32(&v_full[j & 1]), (j >> 1) & 1, p.err)) { alive = false; break; }
                 if (key0 + r >= kv_len) {
 #pragma unroll
@@ -610,6 +591,24 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 }
                 fence_async_smem();
             }
+            // P = 2^(s*sc - m_ref), packed to fp16 over the first 64 columns of
+            // S (column 16c+i holds keys 32c+2i, 32c+2i+1)
+            const float mneg = m_ref == -INFINITY ? 0.f : -m_ref;
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < kTcKeys / 32; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float a0 = ex2(fmaf(v[c][i], sc, mneg));
+                    const float a1 = ex2(fmaf(v[c][i + 1], sc, mneg));
+                    sum4[(i >> 1) & 3] += a0 + a1;
+                    pk[i >> 1] = pack_half2(a0, a1);
+                }
+                tmem_st16(lane_base + s_col + c * 16, pk);
+            }
+            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&p_full[t]));
         }
