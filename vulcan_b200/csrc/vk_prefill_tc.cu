@@ -122,9 +122,9 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     uint64_t* v_full = bars + 4;   // [2]
     uint64_t* v_empty = bars + 6;  // [2]
     uint64_t* s_full = bars + 8;   // [tile]   S of the tile written
-    uint64_t* p_full = bars + 10;  // [tile]   P written, O rescaled (count 128)
+    uint64_t* p_full = bars + 10;  // [tile]   P written, O rescaled (one arrival per softmax warp of the tile)
     uint64_t* o_full = bars + 12;  // [tile]   PV of the tile done
-    uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (count 256)
+    uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (one arrival per softmax warp)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     uint64_t* stg_full = bars + 17;   // FP8 [K, V]: the tile's K (V) codes and scales are staged
     uint64_t* stg_empty = bars + 19;  // FP8 [K, V]: the converters are done with them
@@ -159,10 +159,10 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
         for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&bars[i]), 1);
         for (int t = 0; t < 2; ++t) {
             mbar_init(smem_u32(&s_full[t]), 1);
-            mbar_init(smem_u32(&p_full[t]), 128);
+            mbar_init(smem_u32(&p_full[t]), 4);
             mbar_init(smem_u32(&o_full[t]), 1);
         }
-        mbar_init(smem_u32(q_full), 256);
+        mbar_init(smem_u32(q_full), 8);
         if (FMT) {
             for (int hf = 0; hf < 2; ++hf) {
                 mbar_init(smem_u32(&stg_full[hf]), 1);
@@ -524,7 +524,8 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                              : "memory");
             }
             fence_async_smem();
-            mbar_arrive(smem_u32(q_full));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(q_full));
         }
         const float sc = p.scale_log2;
         float m_ref = -INFINITY, l = 0.f;  // m_ref in the scaled (log2) domain
@@ -609,8 +610,11 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
             }
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             tmem_wait_st();
+            // tcgen05.wait::st above is warp-collective: the warp's P and O
+            // stores are complete when lane 0 signals for the warp
             tc_fence_before();
-            mbar_arrive(smem_u32(&p_full[t]));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&p_full[t]));
         }
         if (alive && ntt > 0 && wait_warp(smem_u32(&o_full[t]), (ntt - 1) & 1, p.err)) {
             tc_fence_after();
