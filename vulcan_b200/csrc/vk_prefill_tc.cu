@@ -562,20 +562,6 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 alpha = ex2(m_ref - m_new);
                 m_ref = m_new;
             }
-            // tcgen05.ld/st are warp-collective: rescale O if any row of the warp
-            // needs it (PV of the previous tile completed before this S was written), before any
-            // PV of this tile starts
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-                for (int c = 0; c < kTcD / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(lane_base + o_col + c * 32, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] *= alpha;
-                    tmem_st32(lane_base + o_col + c * 32, v);
-                }
-            }
             if (!FMT && j == ntiles - 1 && key0 + kTcKeys > kv_len) {
                 // the CTA's last key tile: zero V rows of keys at or beyond the
                 // written length before any PV of it (both tiles may do it; same
@@ -609,6 +595,23 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 tmem_st16(lane_base + s_col + c * 16, pk);
             }
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            // tcgen05.ld/st are warp-collective: rescale O if any row of the warp
+            // needs it (PV of the previous tile completed before this S was written), before the
+            // PV of this tile starts.  Done after P is stored, when the S row's
+            // 128 registers are dead: the kernel's 10 warps get 168 registers a
+            // thread, and rescaling with the row still live spilled ~280 bytes
+            // into the max pass (677 -> 765 TFLOP/s on the 7B chunked prefill).
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < kTcD / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(lane_base + o_col + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] *= alpha;
+                    tmem_st32(lane_base + o_col + c * 32, v);
+                }
+            }
             tmem_wait_st();
             // tcgen05.wait::st above is warp-collective: the warp's P and O
             // stores are complete when lane 0 signals for the warp
