@@ -19,7 +19,9 @@
 //    tcgen05.commit arrivals on mbarriers; a K or V stage is released by the
 //    commit after the last MMA that reads it.
 //  * warp 8 lane 0 streams K and V pages with 2-D TMA boxes of 16 rows x 128 B
-//    (128-byte swizzle) into separate 2-stage rings.
+//    (128-byte swizzle) into separate 2-stage rings; a key tile's K and V land
+//    on one barrier, so the issuer takes one data wait per key tile (its waits
+//    cost ~200 cycles each even when the phase has long completed).
 //  * warps 0-3 (tile A) and 4-7 (tile B): one thread per query row (its TMEM
 //    lane).  Per key tile: the S row read from TMEM once into registers, its
 //    max (masked on the causal diagonal), P = 2^(s*scale - m) packed to fp16
@@ -117,9 +119,9 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     const uint32_t sbase = smem_u32(smem);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (FMT ? kTcBar8 : kTcBar));
     // barrier slots
-    uint64_t* k_full = bars + 0;   // [2]
+    uint64_t* k_full = bars + 0;   // [2]  fp16 pages: K and V of the stage landed; FP8: K converted
     uint64_t* k_empty = bars + 2;  // [2]
-    uint64_t* v_full = bars + 4;   // [2]
+    uint64_t* v_full = bars + 4;   // [2]  FP8 pages: V converted
     uint64_t* v_empty = bars + 6;  // [2]
     uint64_t* s_full = bars + 8;   // [tile]   S of the tile written
     uint64_t* p_full = bars + 10;  // [tile]   P written, O rescaled (one arrival per softmax warp of the tile)
@@ -404,15 +406,14 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                     }
                     pages[i] = pg;
                 }
-                for (int kv = 0; kv < 2 && ok; ++kv) {  // K ring, then V ring
-                    uint64_t* full = kv ? v_full : k_full;
+                for (int kv = 0; kv < 2 && ok; ++kv) {  // K ring, then V ring; both land on k_full
                     uint64_t* empty = kv ? v_empty : k_empty;
                     if (j >= 2 && !mbar_wait(smem_u32(&empty[st]), ((j >> 1) - 1) & 1, p.err)) {
                         ok = false;
                         break;
                     }
-                    const uint32_t bar = smem_u32(&full[st]);
-                    mbar_expect_tx(bar, npg * 2 * (P * 128));
+                    const uint32_t bar = smem_u32(&k_full[st]);
+                    if (kv == 0) mbar_expect_tx(bar, 2 * npg * 2 * (P * 128));
                     const uint32_t dst0 = sbase + (kv ? kTcV : kTcK) + st * 32768;
                     for (int i = 0; i < npg; ++i) {
                         const int row = ((p.layer * p.num_pages + pages[i]) * p.Hkv + hkv) * (2 * P) + kv * P;
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 // before the softmax ends) measured 3% slower, the spinning issuer
                 // taking issue slots from the softmax warps of its sub-partition.
                 ok = ok && mbar_wait(smem_u32(&p_full[t]), j & 1, p.err);
-                if (t == 0 || j >= ntA) ok = ok && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
+                if (FMT && (t == 0 || j >= ntA)) ok = ok && mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, p.err);
                 if (!ok) return;
                 tc_fence_after();
                 const uint64_t dv = dv0 + static_cast<uint64_t>(st * (32768 >> 4));
@@ -566,7 +567,7 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
                 // the CTA's last key tile: zero V rows of keys at or beyond the
                 // written length before any PV of it (both tiles may do it; same
                 // zeros)
-                if (!wait_warp(smem_u32(&v_full[j & 1]), (j >> 1) & 1, p.err)) { alive = false; break; }
+                if (!wait_warp(smem_u32(&k_full[j & 1]), (j >> 1) & 1, p.err)) { alive = false; break; }
                 if (key0 + r >= kv_len) {
 #pragma unroll
                     for (int hb = 0; hb < 2; ++hb)
