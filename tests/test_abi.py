@@ -56,6 +56,7 @@ def test_host_side_argument_checks():
     assert lib.vk_page_ptr(None, 0) is None
     assert lib.vk_pages_in_use(None) == 0
     assert lib.vk_decode(None, 0, None, None, None, 1, None, 1, 1, 16, 0.0, None, 0, None) == _lib.VK_INVALID_ARG
+    assert lib.vk_set_decode_workers(None, 4) == _lib.VK_INVALID_ARG
     assert lib.vk_attention_f32(None, None, None, None, 1, 1, 4, 512, None) == _lib.VK_UNSUPPORTED
     assert lib.vk_attention_f32(None, None, None, None, 1, 1, 4, 8, None) == _lib.VK_INVALID_ARG
     assert lib.vk_attention_f32(None, None, None, None, 0, 1, 4, 8, None) == _lib.VK_OK  # empty
