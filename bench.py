@@ -1063,12 +1063,17 @@ def run_prefill(args, wl):
 def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws, dev, world, gathered, comm,
             lens_host, plan_ws, use_graph, gat=None):
     """Same step through the public API with host buffers: each layer's q/k/v is
-    copied from pinned host memory to the device on a copy stream (double
-    buffered, overlapping the previous layer's kernel; they stand in for the
-    projections a model computes on the device), and every layer's attention
-    output (this rank's heads) is copied back to pinned host memory on a second
-    copy stream, plus the last layer's all-gathered output when heads are
-    sharded, all inside the timed region.  At N=1 the step is one CUDA graph."""
+    copied from pinned host memory to the device on a copy stream (they stand
+    in for the projections a model computes on the device), and every layer's
+    attention output (this rank's heads) is copied back to pinned host memory
+    on a second copy stream, plus the last layer's all-gathered output when
+    heads are sharded, all inside the timed region.  The layers run in chunks
+    of growing size (1, 2, 4, 8, 16, ..., the last layer alone): a chunk's
+    inputs are copied while the previous chunk runs, its kernels run back to
+    back with early start, and its outputs are copied back after its last
+    kernel, so only the first layer's inputs and the last layer's output are
+    not hidden.  (NCCL all-gather: one layer at a time, double buffered.)  At
+    N=1 the step is one CUDA graph."""
     import torch
     import torch.distributed as dist
     g = torch.Generator()
@@ -1080,7 +1085,8 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     out_shape = (world, Bl, hq_l, D) if gathered_host else (Bl, hq_l, D)
     hout = torch.empty(out_shape, dtype=torch.float16).pin_memory()
     hout_layers = torch.empty(L, Bl, hq_l, D, dtype=torch.float16).pin_memory()  # every layer, own heads
-    nbuf = 2
+    chunked = gathered is None  # NCCL all-gather keeps one layer at a time
+    nbuf = L if chunked else 2
     dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
     dk = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
     dv = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
@@ -1094,9 +1100,22 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     d2h_bytes = hout_layers.numel() * 2 + (hout.numel() * 2 if gathered_host else 0)
     plan_keep = {}
 
+    chunks = []  # (first layer, layers): growing sizes, the last layer alone
+    c0, size = 0, 1
+    while c0 < L:
+        n = min(size, L - c0)
+        chunks.append((c0, n))
+        c0 += n
+        size = min(2 * size, 16)
+    if chunks[-1][1] > 1:
+        f, n = chunks.pop()
+        chunks += [(f, n - 1), (L - 1, 1)]
+
     def new_plan(parity=0):
         if args.path == "planned":
             p_ = pool.plan(lens_host, hq_l, workspace=plan_ws)
+            if chunked and not args.no_early_start:
+                p_.set_early_start(True)  # the layers of a chunk are back to back
             if gat is not None:
                 # alternate steps write alternate halves of the 2L slots, so a
                 # slot is rewritten only after every rank's copies of it are done
@@ -1104,7 +1123,51 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             p_.upload()
             plan_keep["plan"] = p_
 
+    def run_layer(plan, l, s):
+        if plan is None:
+            pool.append(l, dk[s].view(Bl, 1, hkv_l, D), dv[s].view(Bl, 1, hkv_l, D), bt_d, pos_d)
+            pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
+        else:
+            plan.run(l, dq[s], bt_d, out=None if gat is not None else douts[s], k_new=dk[s], v_new=dv[s])
+
+    def layers_chunked(parity=0):
+        base = sched.slot_base(parity + 1)
+        cur = torch.cuda.current_stream(dev)
+        plan = plan_keep.get("plan")
+        h2d.wait_stream(cur)  # the previous step's kernels have read every input buffer
+        d2h.wait_stream(cur)
+        loaded = []
+        with torch.cuda.stream(h2d):
+            for c0, n in chunks:
+                for l in range(c0, c0 + n):
+                    dq[l].copy_(hq[l], non_blocking=True)
+                    dk[l].copy_(hk[l], non_blocking=True)
+                    dv[l].copy_(hv[l], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                loaded.append(e)
+        for ci, (c0, n) in enumerate(chunks):
+            cur.wait_event(loaded[ci])
+            for l in range(c0, c0 + n):
+                run_layer(plan, l, l)
+            fe = torch.cuda.Event()
+            fe.record(cur)
+            d2h.wait_event(fe)
+            with torch.cuda.stream(d2h):
+                for l in range(c0, c0 + n):
+                    if gat is not None:
+                        hout_layers[l].copy_(gat.view(base + l, Bl, hq_l, D)[gat.rank], non_blocking=True)
+                        if l == L - 1:
+                            plan.gather_wait(l, stream=d2h)  # every rank's slices of the step
+                            hout.copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
+                    else:
+                        hout_layers[l].copy_(douts[l], non_blocking=True)
+        cur.wait_stream(d2h)  # outputs read before the next step rewrites them
+        cur.wait_stream(h2d)
+
     def layers(parity=0):
+        if chunked:
+            return layers_chunked(parity)
         base = sched.slot_base(parity + 1)
         cur = torch.cuda.current_stream(dev)
         plan = plan_keep.get("plan")
@@ -1134,11 +1197,7 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             cur.wait_event(loaded[s])
             if outdone[s] is not None:
                 cur.wait_event(outdone[s])
-            if plan is None:
-                pool.append(l, dk[s].view(Bl, 1, hkv_l, D), dv[s].view(Bl, 1, hkv_l, D), bt_d, pos_d)
-                pool.decode(l, dq[s], bt_d, lens_d, max_len, out=douts[s], workspace=ws)
-            else:
-                plan.run(l, dq[s], bt_d, out=None if gat is not None else douts[s], k_new=dk[s], v_new=dv[s])
+            run_layer(plan, l, s)
             fe = torch.cuda.Event()
             fe.record(cur)
             freed[s] = fe
@@ -1233,6 +1292,9 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
                     "layer's attention output (this rank's heads) back to pinned host memory" +
                     (", and the last layer's all-gathered output" if gathered_host else "") +
                     "; H2D and D2H on copy streams inside the timed region" +
+                    ("; layers in chunks of %s, each chunk's copies overlapping the previous chunk's kernels, "
+                     "early start within a chunk" % "/".join(str(n) for _, n in chunks) if chunked else
+                     "; one layer at a time, double buffered") +
                     ("; CUDA graph per step" if use_graph else "")}
 
 
