@@ -22,6 +22,11 @@
 //    (128-byte swizzle) into separate 2-stage rings; a key tile's K and V land
 //    on one barrier, so the issuer takes one data wait per key tile (its waits
 //    cost ~200 cycles each even when the phase has long completed).
+//  * Q: both 128-row tiles arrive by TMA (a 3-D map over [tokens][heads][d]
+//    made per call) issued by thread 0 as soon as the barriers exist, so Q
+//    lands together with the first K/V tile; with RoPE the softmax threads
+//    rotate their rows in shared memory before Q is released to the MMAs.
+//    (q not 16-byte aligned: the softmax threads load their rows instead.)
 //  * warps 0-3 (tile A) and 4-7 (tile B): one thread per query row (its TMEM
 //    lane).  Per key tile: the S row read from TMEM once into registers, its
 //    max (masked on the causal diagonal), P = 2^(s*scale - m) packed to fp16
@@ -86,6 +91,7 @@ struct TcParams {
     // FP8 pages: block of (layer, page, head) at pool_base + layer_off + page * seg_bytes + head * head_bytes
     const char* pool_base;
     uint64_t layer_off, seg_bytes, head_bytes;
+    int q_tma;  // 1: Q tiles arrive by TMA (q 16-byte aligned); 0: loaded by the softmax warps
 };
 
 // 3-input max (one instruction on sm_100)
@@ -111,6 +117,7 @@ __device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, uint32_
 
 template <int FMT>
 __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap16,
+                                                                  const __grid_constant__ CUtensorMap tmapq,
                                                                   const TcParams p) {
     constexpr int P = kPageTokens;
     constexpr int NTHR = FMT ? kTcThreads8 : kTcThreads;
@@ -126,7 +133,8 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     uint64_t* s_full = bars + 8;   // [tile]   S of the tile written
     uint64_t* p_full = bars + 10;  // [tile]   P written, O rescaled (one arrival per softmax warp of the tile)
     uint64_t* o_full = bars + 12;  // [tile]   PV of the tile done
-    uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (one arrival per softmax warp)
+    uint64_t* q_full = bars + 14;  // Q of both tiles in shared memory (by TMA without RoPE, else one arrival per softmax warp)
+    uint64_t* q_land = bars + 15;  // Q tiles landed by TMA, before RoPE is applied in shared memory
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
     uint64_t* stg_full = bars + 17;   // FP8 [K, V]: the tile's K (V) codes and scales are staged
     uint64_t* stg_empty = bars + 19;  // FP8 [K, V]: the converters are done with them
@@ -164,7 +172,8 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
             mbar_init(smem_u32(&p_full[t]), 4);
             mbar_init(smem_u32(&o_full[t]), 1);
         }
-        mbar_init(smem_u32(q_full), 8);
+        mbar_init(smem_u32(q_full), (p.q_tma && p.rope_freq == nullptr) ? 1 : 8);
+        mbar_init(smem_u32(q_land), 1);
         if (FMT) {
             for (int hf = 0; hf < 2; ++hf) {
                 mbar_init(smem_u32(&stg_full[hf]), 1);
@@ -172,6 +181,19 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
             }
         }
         mbar_fence_init();
+        if (p.q_tma) {
+            // both 128-row Q tiles, two 64-column halves each (128-byte swizzle:
+            // the layout the MMA descriptors read); rows past the chunk read the
+            // next rows of q or zeros, and are never stored
+            const uint32_t bar = smem_u32(p.rope_freq == nullptr ? q_full : q_land);
+            prefetch_tmap(&tmapq);
+            mbar_expect_tx(bar, 2 * 2 * kTcRows * 128);
+            const uint64_t pol = l2_evict_first_policy();
+            for (int t = 0; t < 2; ++t)
+                for (int hb = 0; hb < 2; ++hb)
+                    tma_load_3d(sbase + kTcQ + t * 32768 + hb * 16384, &tmapq, hb * 64, h, b * p.T + q0 + t * kTcRows,
+                                bar, pol);
+        }
     }
     // zero both V stages: rows a last tile does not load keep finite values
     for (int i = threadIdx.x; i < 2 * 32768 / 16; i += NTHR)
@@ -504,8 +526,30 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
         const int ntt = t ? ntB : ntA;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
         const uint32_t s_col = t * 128, o_col = 256 + t * 128;
+        bool alive0 = true;
         // Q row -> shared memory (K-major, 128-byte swizzle)
-        {
+        if (p.q_tma && p.rope_freq != nullptr) {
+            // landed by TMA: rotate this thread's row in place
+            if (!wait_warp(smem_u32(q_land), 0, p.err)) alive0 = false;
+            if (alive0) {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const uint32_t addr =
+                        sbase + kTcQ + t * 32768 + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                    uint4 v;
+                    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                                 : "r"(addr));
+                    v = rope_uint4(v, c * 8, qpos, p.rope_freq);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                                 "r"(v.w)
+                                 : "memory");
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(q_full));
+        } else if (!p.q_tma) {
             const uint4* src = reinterpret_cast<const uint4*>(
                 p.q + ((static_cast<int64_t>(b) * p.T + (valid_row ? qrow : 0)) * p.Hq + h) * kTcD);
             // all 16 loads first: a shared store (asm with a memory clobber)
@@ -530,7 +574,7 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
         }
         const float sc = p.scale_log2;
         float m_ref = -INFINITY, l = 0.f;  // m_ref in the scaled (log2) domain
-        bool alive = true;
+        bool alive = alive0;
         for (int j = 0; j < ntt && alive; ++j) {
             if (!wait_warp(smem_u32(&s_full[t]), j & 1, p.err)) { alive = false; break; }
             tc_fence_after();
@@ -651,7 +695,7 @@ __global__ void __launch_bounds__(FMT ? kTcThreads8 : kTcThreads, 1) prefill_tc_
     }
 }
 
-vk_status launch_prefill_tc(vk_pool* pool, const TcParams& p, int B, cudaStream_t st) {
+vk_status launch_prefill_tc(vk_pool* pool, const TcParams& p, const CUtensorMap& tq, int B, cudaStream_t st) {
     static uint64_t attr_set[2] = {0, 0};
     const int fmt = pool->kv_format == VK_KV_FP8 ? 1 : 0;
     const uint64_t bit = 1ull << (pool->device & 63);
@@ -661,8 +705,8 @@ vk_status launch_prefill_tc(vk_pool* pool, const TcParams& p, int B, cudaStream_
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(prefill_tc)");
         attr_set[fmt] |= bit;
     }
-    if (fmt) prefill_tc_kernel<1><<<dim3(p.Hq * B, p.q_tiles), kTcThreads8, kTcSmem8, st>>>(pool->tmap16, p);
-    else prefill_tc_kernel<0><<<dim3(p.q_tiles, p.Hq, B), kTcThreads, kTcSmem, st>>>(pool->tmap16, p);
+    if (fmt) prefill_tc_kernel<1><<<dim3(p.Hq * B, p.q_tiles), kTcThreads8, kTcSmem8, st>>>(pool->tmap16, tq, p);
+    else prefill_tc_kernel<0><<<dim3(p.q_tiles, p.Hq, B), kTcThreads, kTcSmem, st>>>(pool->tmap16, tq, p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? VK_OK : cuda_fail(e, "prefill_tc_kernel launch");
 }
@@ -690,7 +734,25 @@ vk_status prefill_tc(vk_pool* pool, int layer, const void* q, void* out, const i
     p.layer_off = static_cast<uint64_t>(layer) * pool->seg_stride;
     p.seg_bytes = pool->seg_bytes;
     p.head_bytes = pool->head_bytes;
-    return launch_prefill_tc(pool, p, B, st);
+    // Q by TMA: a 3-D view [B*T tokens][Hq heads][128 d] of q, boxes of 64 d x
+    // 1 head x 128 tokens; needs q 16-byte aligned (else the softmax warps load it)
+    alignas(64) CUtensorMap tq = pool->tmap16;  // placeholder when unused
+    p.q_tma = 0;
+    auto encode = tmap_encode_fn();
+    const uint64_t ntok = static_cast<uint64_t>(B) * T;
+    if (encode && !(reinterpret_cast<uintptr_t>(q) & 15) && ntok + 2 * kTcRows < (1ull << 31)) {
+        cuuint64_t dims[3] = {static_cast<cuuint64_t>(kTcD), static_cast<cuuint64_t>(Hq), ntok};
+        cuuint64_t strides[2] = {static_cast<cuuint64_t>(kTcD) * 2, static_cast<cuuint64_t>(Hq) * kTcD * 2};
+        cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kTcRows)};
+        cuuint32_t estr[3] = {1, 1, 1};
+        if (encode(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+            p.q_tma = 1;
+        else
+            tq = pool->tmap16;
+    }
+    return launch_prefill_tc(pool, p, tq, B, st);
 }
 
 }  // namespace vk
