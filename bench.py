@@ -157,7 +157,7 @@ def measured_peaks():
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
 # the committed ncu captures, for the workloads they were taken on.
-NCU_DECODE_70B_BYTES = 590.999296e6 + 4.925184e6   # profiles/planned_decode_kernel_70b-one-layer_full.md
+NCU_DECODE_70B_BYTES = 591.055360e6 + 4.537344e6   # profiles/planned_decode_kernel_70b-one-layer_full.md
 NCU_PREFILL_2SEQ_BYTES = 189.434624e6 + 8.898816e6  # profiles/prefill_tc_kernel_small-case_full.md
 
 
