@@ -1087,10 +1087,12 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
     hout_layers = torch.empty(L, Bl, hq_l, D, dtype=torch.float16).pin_memory()  # every layer, own heads
     chunked = gathered is None  # NCCL all-gather keeps one layer at a time
     nbuf = L if chunked else 2
-    dq = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    dk = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    dv = [torch.empty(Bl, hkv_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
-    douts = [torch.empty(Bl, hq_l, D, device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    # one device tensor per input / output across the buffered layers, so a
+    # chunk's copies are one copy per tensor
+    dq = torch.empty(nbuf, Bl, hq_l, D, device=dev, dtype=torch.float16)
+    dk = torch.empty(nbuf, Bl, hkv_l, D, device=dev, dtype=torch.float16)
+    dv = torch.empty(nbuf, Bl, hkv_l, D, device=dev, dtype=torch.float16)
+    douts = torch.empty(nbuf, Bl, hq_l, D, device=dev, dtype=torch.float16)
     h2d = torch.cuda.Stream(device=dev)
     d2h = torch.cuda.Stream(device=dev)
     compute = torch.cuda.current_stream(dev)
@@ -1139,10 +1141,9 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
         loaded = []
         with torch.cuda.stream(h2d):
             for c0, n in chunks:
-                for l in range(c0, c0 + n):
-                    dq[l].copy_(hq[l], non_blocking=True)
-                    dk[l].copy_(hk[l], non_blocking=True)
-                    dv[l].copy_(hv[l], non_blocking=True)
+                dq[c0:c0 + n].copy_(hq[c0:c0 + n], non_blocking=True)
+                dk[c0:c0 + n].copy_(hk[c0:c0 + n], non_blocking=True)
+                dv[c0:c0 + n].copy_(hv[c0:c0 + n], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(h2d)
                 loaded.append(e)
@@ -1154,14 +1155,13 @@ def run_e2e(args, pool, L, Bl, hq_l, hkv_l, D, bt_d, pos_d, lens_d, max_len, ws,
             fe.record(cur)
             d2h.wait_event(fe)
             with torch.cuda.stream(d2h):
-                for l in range(c0, c0 + n):
-                    if gat is not None:
-                        hout_layers[l].copy_(gat.view(base + l, Bl, hq_l, D)[gat.rank], non_blocking=True)
-                        if l == L - 1:
-                            plan.gather_wait(l, stream=d2h)  # every rank's slices of the step
-                            hout.copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
-                    else:
-                        hout_layers[l].copy_(douts[l], non_blocking=True)
+                if gat is None:
+                    hout_layers[c0:c0 + n].copy_(douts[c0:c0 + n], non_blocking=True)
+                for l in range(c0, c0 + n) if gat is not None else ():
+                    hout_layers[l].copy_(gat.view(base + l, Bl, hq_l, D)[gat.rank], non_blocking=True)
+                    if l == L - 1:
+                        plan.gather_wait(l, stream=d2h)  # every rank's slices of the step
+                        hout.copy_(gat.view(base + l, Bl, hq_l, D), non_blocking=True)
         cur.wait_stream(d2h)  # outputs read before the next step rewrites them
         cur.wait_stream(h2d)
 
